@@ -1,0 +1,267 @@
+"""Generate the golden fixtures under tests/golden/ by running the REFERENCE itself.
+
+Run in the build container, where the reference checkout and transformers 5.5.0
+are importable (``MICROGEN_REFERENCE`` points at the checkout, default
+``/root/reference``)::
+
+    python tests/golden/make_golden.py
+
+Every array written here is an output of the reference's own code:
+
+* ``quant_cases.npz``   — ``quantize_linear_layer_per_channel``
+  (``microgen/backends/quantized.py:30-39``) on seeded and edge-case matrices;
+  ``quant_digest.json`` — sha256 of codes+scales for a full Llama-3.2-3B-shaped
+  q_proj (3072×3072, N(0, 0.02)), too large to store.
+* ``linear_cases.npz``  — ``QuantizedLinear.forward`` (``quantized.py:24-27``)
+  and ``ColumnParallelLinear`` / ``RowParallelLinear`` (``parallel.py:12-81``)
+  on the dequantized weights, world sizes 2 and 3 (uneven split).
+* ``attn_cases.npz``    — decode attention as the reference computes it:
+  ``KVCacheState.update`` (``runtime/kv_cache.py:76-127``) then HF
+  ``sdpa_attention_forward``; block tables drawn from the reference
+  ``PagedKVCacheAllocator`` (``runtime/paged_kv.py``) after a seeded shuffle of its
+  free list, and the paged pools filled from the contiguous cache.
+* ``alloc_trace.json``  — block ids the reference allocator hands out for a
+  scripted allocate / append / free sequence.
+* ``model_<family>.npz``— a greedy stream of 64 tokens and the logits of its
+  first steps from ``QuantizedPyTorchBackend`` (``quantized.py:41-73``)
+  ``prefill``/``decode`` on seeded tiny Llama / Qwen2 / GPT-2 models. For GPT-2
+  the Conv1D projections are first rewrapped as ``nn.Linear`` (weight =
+  ``Conv1D.weight.T``), because the reference quantizer only swaps ``nn.Linear``.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import random
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("MICROGEN_REFERENCE", "/root/reference")
+sys.path.insert(0, REF)
+sys.path.insert(0, ROOT)  # this repository's ``tests`` package wins over the reference's
+
+from microgen.backends.quantized import (QuantizedPyTorchBackend,  # noqa: E402
+                                         quantize_linear_layer_per_channel)
+from microgen.backends.parallel import ColumnParallelLinear, RowParallelLinear  # noqa: E402
+from microgen.runtime.kv_cache import KVCacheState  # noqa: E402
+from microgen.runtime.paged_kv import PagedKVCacheAllocator  # noqa: E402
+from transformers.integrations.sdpa_attention import sdpa_attention_forward  # noqa: E402
+
+from tests._hf_models import TINY, make_hf_model, prompt_ids  # noqa: E402
+
+torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+
+def ref_quantize(w: np.ndarray):
+    lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(w))
+    ql = quantize_linear_layer_per_channel(lin)
+    return ql, ql.weight_int8.numpy().copy(), ql.scales.numpy().reshape(-1).copy()
+
+
+def edge_matrix() -> np.ndarray:
+    rng = np.random.default_rng(7)
+    w = (rng.standard_normal((8, 48), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    w[0] = 0.0                                                  # all-zero row: scale clamps to 1e-8
+    w[1] = 0.0
+    w[1, :9] = np.array([127, 0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 126.5, -126.5], np.float32)  # exact ties (scale 1)
+    w[2] = np.float32(1e-9) * np.arange(48, dtype=np.float32)  # tiny row: scale floor
+    w[3] = 0.0
+    w[3, 5] = -3.0                                              # single negative extreme
+    w[4] *= np.float32(1e6)                                     # large magnitudes
+    w[5] = np.float32(1e-7)                                     # constant row below the floor*127
+    w[6, ::2] = -w[6, 1::2]                                     # symmetric pairs
+    w[7] = np.linspace(-1, 1, 48, dtype=np.float32)
+    return w
+
+
+def make_quant():
+    cases = {}
+    rng = np.random.default_rng(1)
+    mats = {
+        "seeded": (rng.standard_normal((64, 96), dtype=np.float32) * np.float32(0.02)).astype(np.float32),
+        "edge": edge_matrix(),
+        "wide": (rng.standard_normal((5, 4096), dtype=np.float32) * np.float32(0.02)).astype(np.float32),
+        "ragged": (rng.standard_normal((3, 16), dtype=np.float32)).astype(np.float32),
+    }
+    for name, w in mats.items():
+        _, q, s = ref_quantize(w)
+        cases[f"{name}_w"], cases[f"{name}_q"], cases[f"{name}_s"] = w, q, s
+    np.savez_compressed(os.path.join(HERE, "quant_cases.npz"), **cases)
+
+    # Size-independent property for the full-size matrix: digest of the reference's output.
+    g = torch.Generator().manual_seed(3)
+    w = (torch.randn(3072, 3072, generator=g, dtype=torch.float32) * 0.02)
+    lin = torch.nn.Linear(3072, 3072, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    ql = quantize_linear_layer_per_channel(lin)
+    h = hashlib.sha256()
+    h.update(ql.weight_int8.numpy().tobytes())
+    h.update(ql.scales.numpy().astype(np.float32).tobytes())
+    wd = hashlib.sha256(w.numpy().tobytes()).hexdigest()
+    with open(os.path.join(HERE, "quant_digest.json"), "w") as f:
+        json.dump({"generator": "torch.Generator().manual_seed(3); randn(3072,3072)*0.02 fp32",
+                   "weight_sha256": wd, "codes_scales_sha256": h.hexdigest(),
+                   "code_hist_minus127_0_127": [int((ql.weight_int8 == -127).sum()), int((ql.weight_int8 == 0).sum()),
+                                                int((ql.weight_int8 == 127).sum())]}, f, indent=1)
+
+
+def make_linear():
+    out = {}
+    rng = np.random.default_rng(2)
+    for tag, (M, K, N) in {"a": (5, 96, 40), "b": (1, 64, 33), "c": (8, 160, 72)}.items():
+        w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        b = (rng.standard_normal(N, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+        x = rng.standard_normal((M, K), dtype=np.float32)
+        lin = torch.nn.Linear(K, N)
+        with torch.no_grad():
+            lin.weight.copy_(torch.from_numpy(w))
+            lin.bias.copy_(torch.from_numpy(b))
+        ql = quantize_linear_layer_per_channel(lin)
+        xt = torch.from_numpy(x)
+        with torch.no_grad():
+            y = ql(xt).numpy()
+            wdq = (ql.weight_int8.float() * ql.scales).clone()
+            res = {}
+            for world in (2, 3):
+                col = ColumnParallelLinear(wdq, lin.bias.data, world)
+                row = RowParallelLinear(wdq, lin.bias.data, world)
+                res[f"col{world}"] = col(xt).numpy()
+                res[f"row{world}"] = row(xt).numpy()
+        out.update({f"{tag}_x": x, f"{tag}_w": w, f"{tag}_b": b, f"{tag}_q": ql.weight_int8.numpy(),
+                    f"{tag}_s": ql.scales.numpy().reshape(-1), f"{tag}_y": y})
+        out.update({f"{tag}_{k}": v for k, v in res.items()})
+    np.savez_compressed(os.path.join(HERE, "linear_cases.npz"), **out)
+
+
+class _Attn(torch.nn.Module):
+    def __init__(self, groups):
+        super().__init__()
+        self.num_key_value_groups = groups
+        self.is_causal = True
+
+
+def make_attn():
+    out = {}
+    cases = {
+        "gqa": dict(B=3, Hq=8, Hkv=2, D=64, ctx=[1, 17, 40], blocks=16, seed=11),
+        "mha": dict(B=2, Hq=4, Hkv=4, D=32, ctx=[16, 33], blocks=8, seed=12),
+        "llama": dict(B=2, Hq=24, Hkv=8, D=128, ctx=[50, 128], blocks=16, seed=13),
+    }
+    for tag, c in cases.items():
+        B, Hq, Hkv, D, ctx = c["B"], c["Hq"], c["Hkv"], c["D"], c["ctx"]
+        rng = np.random.default_rng(c["seed"])
+        L = max(ctx)
+        q = rng.standard_normal((B, Hq, D), dtype=np.float32)
+        k = rng.standard_normal((B, Hkv, L, D), dtype=np.float32)
+        v = rng.standard_normal((B, Hkv, L, D), dtype=np.float32)
+        alloc = PagedKVCacheAllocator(num_blocks=c["blocks"] * B, block_size=16)
+        random.Random(c["seed"]).shuffle(alloc._free_blocks)
+        maxb = (L + 15) // 16
+        tables = np.zeros((B, maxb), np.int32)
+        kpool = np.zeros((alloc.num_blocks, Hkv, 16, D), np.float32)
+        vpool = np.zeros_like(kpool)
+        outs = np.zeros((B, Hq, D), np.float32)
+        for b in range(B):
+            bt = alloc.allocate_sequence(f"s{b}", ctx[b])
+            ids = [blk.block_id for blk in bt.physical_blocks]
+            tables[b, :len(ids)] = ids
+            for t in range(ctx[b]):
+                kpool[ids[t // 16], :, t % 16] = k[b, :, t]
+                vpool[ids[t // 16], :, t % 16] = v[b, :, t]
+            # reference: contiguous cache grown by KVCacheState.update, then HF SDPA for one query token
+            cache = KVCacheState(max_seq_len=4096)
+            kk = torch.from_numpy(k[b:b + 1, :, :ctx[b]])
+            vv = torch.from_numpy(v[b:b + 1, :, :ctx[b]])
+            split = max(1, ctx[b] // 2)
+            cache.update(kk[:, :, :split], vv[:, :, :split], 0)
+            kc, vc = cache.update(kk[:, :, split:], vv[:, :, split:], 0) if ctx[b] > split else (kk, vv)
+            qq = torch.from_numpy(q[b:b + 1, :, None, :])
+            o, _ = sdpa_attention_forward(_Attn(Hq // Hkv), qq, kc, vc, None, scaling=1.0 / np.sqrt(D))
+            outs[b] = o[0, 0].numpy()
+        out.update({f"{tag}_q": q, f"{tag}_kpool": kpool, f"{tag}_vpool": vpool, f"{tag}_tables": tables,
+                    f"{tag}_ctx": np.array(ctx, np.int32), f"{tag}_out": outs})
+    np.savez_compressed(os.path.join(HERE, "attn_cases.npz"), **out)
+
+
+def make_alloc_trace():
+    a = PagedKVCacheAllocator(num_blocks=12, block_size=16)
+    trace = []
+    t1 = a.allocate_sequence("a", 35)
+    trace.append(("alloc", "a", 35, [b.block_id for b in t1.physical_blocks]))
+    t2 = a.allocate_sequence("b", 16)
+    trace.append(("alloc", "b", 16, [b.block_id for b in t2.physical_blocks]))
+    for _ in range(13):
+        a.append_token(t1)
+    trace.append(("append13", "a", t1.num_tokens, [b.block_id for b in t1.physical_blocks]))
+    a.append_token(t2)
+    trace.append(("append1", "b", t2.num_tokens, [b.block_id for b in t2.physical_blocks]))
+    a.free_sequence(t1)
+    trace.append(("free", "a", a.get_num_free_blocks(), [b.block_id for b in a._free_blocks]))
+    t3 = a.allocate_sequence("c", 70)
+    trace.append(("alloc", "c", 70, [b.block_id for b in t3.physical_blocks]))
+    t4 = a.allocate_sequence("d", 0)
+    trace.append(("alloc", "d", 0, [b.block_id for b in t4.physical_blocks]))
+    err = None
+    try:
+        a.allocate_sequence("e", 16 * 20)
+    except MemoryError as e:
+        err = str(e)
+    trace.append(("oom", "e", 320, err))
+    with open(os.path.join(HERE, "alloc_trace.json"), "w") as f:
+        json.dump(trace, f, indent=1)
+
+
+def _conv1d_to_linear(model):
+    from transformers.pytorch_utils import Conv1D
+
+    def walk(mod):
+        for name, ch in list(mod.named_children()):
+            if isinstance(ch, Conv1D):
+                lin = torch.nn.Linear(ch.weight.shape[0], ch.weight.shape[1])
+                with torch.no_grad():
+                    lin.weight.copy_(ch.weight.t())
+                    lin.bias.copy_(ch.bias)
+                setattr(mod, name, lin)
+            else:
+                walk(ch)
+    walk(model)
+
+
+def make_models(n_prompt=16, n_new=64, n_logits=8):
+    for fam, shape in TINY.items():
+        model, state = make_hf_model(shape, seed=0)
+        if fam == "gpt2":
+            _conv1d_to_linear(model)
+        be = QuantizedPyTorchBackend(quant_type="int8")
+        be.load_model(f"tiny-{fam}", model_instance=model)
+        prompt = prompt_ids(shape["vocab"], n_prompt, seed=0)
+        ids = torch.tensor([prompt], dtype=torch.long)
+        logits, cache = be.prefill(ids, cache=KVCacheState(max_seq_len=1024))
+        toks, lg = [], []
+        for i in range(n_new):
+            tok = torch.argmax(logits, dim=-1, keepdim=True)
+            toks.append(int(tok.item()))
+            if i < n_logits:
+                lg.append(logits[0].numpy().copy())
+            logits, cache = be.decode(tok, cache=cache)
+        np.savez_compressed(os.path.join(HERE, f"model_{fam}.npz"), prompt=np.array(prompt, np.int64),
+                            tokens=np.array(toks, np.int64), logits=np.stack(lg).astype(np.float32),
+                            shape=json.dumps(shape))
+
+
+if __name__ == "__main__":
+    make_quant()
+    make_linear()
+    make_attn()
+    make_alloc_trace()
+    make_models()
+    print("golden fixtures written to", HERE)
