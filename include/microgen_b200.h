@@ -1,0 +1,117 @@
+/*
+ * libmicrogen_b200 — C ABI of the B200 (sm_100a) decode-step hot path for MicroGen.
+ *
+ * Plain pointers and sizes only. Every device pointer is a CUDA device address of
+ * the current device; `stream` is a cudaStream_t (NULL = legacy default stream).
+ * Every entry point returns an int status (MG_OK = 0) and never aborts or traps;
+ * launches are asynchronous on `stream`. Device-side failures (a bounded wait that
+ * gave up, an index out of range) are recorded in a device error word that
+ * mg_device_error() reads.
+ *
+ * Reference interfaces replaced (paths inside the MicroGen project):
+ *   microgen/backends/quantized.py:30-39   quantize_linear_layer_per_channel -> mg_quantize_rows_i8
+ *   microgen/backends/quantized.py:24-27   QuantizedLinear.forward           -> mg_i8_linear
+ *   microgen/backends/parallel.py:34-37    ColumnParallelLinear.forward      -> mg_i8_linear on the rank's shard
+ *   microgen/backends/parallel.py:65-81    RowParallelLinear.forward (+sum)  -> mg_i8_linear + mg_allreduce_*
+ *   microgen/runtime/kv_cache.py:76-127    KVCacheState.update (torch.cat)   -> mg_rope_kv_append (paged slot write)
+ *   transformers sdpa_attention_forward    decode SDPA over the cache        -> mg_paged_decode_attn
+ *   microgen/backends/pytorch.py:153-155   greedy torch.argmax               -> mg_argmax_rows
+ */
+#ifndef MICROGEN_B200_H
+#define MICROGEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MG_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------------------------ */
+#define MG_OK 0
+#define MG_ERR_INVALID_ARG 1 /* a size, pointer or alignment the kernels do not accept */
+#define MG_ERR_UNSUPPORTED 2 /* a shape outside what the kernels were built for */
+#define MG_ERR_CUDA 3        /* a CUDA runtime call failed (mg_last_cuda_error has the code) */
+#define MG_ERR_TIMEOUT 4     /* a bounded device wait gave up (peer flag, mbarrier) */
+#define MG_ERR_DEVICE 5      /* a device-side check failed (index out of range) */
+
+/* ---- linear epilogues (applied to acc*scale[n] + bias[n]) --------------------------------- */
+#define MG_EPI_STORE_BF16 0  /* y[m*ldy+n] = bf16(v) */
+#define MG_EPI_STORE_F32 1   /* y[m*ldy+n] = v (fp32) */
+#define MG_EPI_ADD_F32 2     /* y[m*ldy+n] += v (fp32 residual stream) */
+#define MG_EPI_SWIGLU_BF16 3 /* rows interleaved in 64-row gate/up groups; y[m*ldy+f] = bf16(silu(g)*u) */
+#define MG_EPI_GELU_BF16 4   /* y[m*ldy+n] = bf16(gelu_tanh(v)) (GPT-2 "gelu_new") */
+
+int mg_abi_version(void);
+const char* mg_status_string(int status);
+/* Last cudaError_t recorded by a failing entry point of this thread (0 if none). */
+int mg_last_cuda_error(void);
+/* Synchronise `stream`, then read (and when `clear` != 0 reset) the device error word.
+ * *code = MG_OK or the first recorded MG_ERR_*; *info = where it was recorded. */
+int mg_device_error(void* stream, int clear, int* code, int* info);
+
+/* ---- INT8 per-output-channel quantization (bit-exact with quantized.py:30-39) -------------- */
+/* w fp32 [n,k] row-major -> q int8 [n,k], scales fp32 [n]:
+ *   s = max(max_k |w| / 127, 1e-8);  q = clamp(rint_half_even(w / s), -128, 127) */
+int mg_quantize_rows_i8(const float* w, int64_t n, int64_t k, int8_t* q, float* scales, void* stream);
+
+/* ---- INT8 weight-only linear (quantized.py:24-27; parallel.py shards) ---------------------- */
+/* y = epilogue( x[m,k] (bf16, row stride ldx) · (q[n,k]·scales[n])ᵀ + bias[n] ), fp32 accumulate.
+ * bias is fp32 [n] or NULL. k % 16 == 0, ldx % 8 == 0, 16-byte aligned x and q.
+ * mg_i8_linear picks the kernel: the tcgen05 tensor-core kernel for every m, unless
+ * MG_EPI_SWIGLU needs n % 128 == 0 and it does not hold. */
+int mg_i8_linear(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
+                 const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, void* stream);
+/* Same contract, CUDA-core kernel (one warp per output row, 128-bit weight loads). */
+int mg_i8_linear_simt(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
+                      const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, void* stream);
+/* Same contract, tcgen05 kernel with an explicit split-K cluster size (1..8; 0 = automatic). */
+int mg_i8_linear_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
+                    const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, int split_k, void* stream);
+
+/* ---- paged KV: RoPE + append (kv_cache.py:76-127, as one slot write per token) ------------ */
+/* qkv fp32 [b, (hq+2*hkv)*d] (row stride ld_qkv): q heads, then k heads, then v heads.
+ * rope: cos_sin fp32 [max_pos, d] (cos of the d/2 frequencies, then sin), NULL = no rotation.
+ * Writes q_out fp32 [b, hq, d] (rotated) and K/V (rotated K) into the pools
+ * bf16 [num_blocks, hkv, 16, d] at slot_mapping[i] = block_id*16 + offset. */
+int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t* positions, const float* cos_sin,
+                      int max_pos, const int32_t* slot_mapping, int b, int hq, int hkv, int d, float* q_out,
+                      void* k_pool, void* v_pool, int64_t num_blocks, void* stream);
+
+/* ---- paged decode attention ---------------------------------------------------------------- */
+/* out bf16 [b, hq*d] = softmax(q·Kᵀ·scale)·V per sequence, query head h reading kv head
+ * h / (hq/hkv); K/V gathered through block_tables int32 [b, max_blocks] from pools
+ * bf16 [num_blocks, hkv, 16, d]; ctx_lens int32 [b] >= 1. d in {64, 128}; hq/hkv <= 16.
+ * n_shared_blocks: the first n_shared_blocks entries of every table are the same blocks
+ * (a shared prefix); they are read once per batch. 0 = no sharing.
+ * workspace: device scratch of mg_paged_attn_workspace_bytes() bytes (may be NULL if 0). */
+int mg_paged_attn_workspace_bytes(int b, int hq, int hkv, int d, int max_blocks, int n_shared_blocks,
+                                  size_t* bytes);
+int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                         const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b, int hq,
+                         int hkv, int d, int n_shared_blocks, float scale, void* out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* ---- small fused ops of the decode step ---------------------------------------------------- */
+/* h fp32 [b, hidden] = wte[tokens[i]] (+ wpe[positions[i]] when wpe != NULL). */
+int mg_embed(const int32_t* tokens, const int32_t* positions, const float* wte, const float* wpe, int b,
+             int hidden, int64_t vocab, int max_pos, float* h, void* stream);
+/* x bf16 [m, n] = w * h * rsqrt(mean(h^2) + eps)  (LlamaRMSNorm / Qwen2RMSNorm) */
+int mg_rmsnorm(const float* h, const float* w, int m, int n, float eps, void* x, void* stream);
+/* x bf16 [m, n] = (h - mean) * rsqrt(var + eps) * w + bias  (GPT-2 LayerNorm) */
+int mg_layernorm(const float* h, const float* w, const float* bias, int m, int n, float eps, void* x,
+                 void* stream);
+/* out[i] = first index of the maximum of logits fp32 row i (row stride ld) — torch.argmax. */
+int mg_argmax_rows(const float* logits, int m, int64_t n, int64_t ld, int32_t* out, void* stream);
+/* One greedy step forward for a graph-replayed decode loop: tokens = next; positions += 1;
+ * ctx_lens += 1; slots = table[pos/16]*16 + pos%16 for the new position. */
+int mg_decode_advance(int32_t* tokens, const int32_t* next_tokens, int32_t* positions, int32_t* ctx_lens,
+                      int32_t* slots, const int32_t* block_tables, int max_blocks, int b, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MICROGEN_B200_H */

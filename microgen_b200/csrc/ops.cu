@@ -1,0 +1,289 @@
+// Per-row kernels of the decode step: the INT8 quantizer, norms, embedding,
+// RoPE + paged KV append, greedy argmax, and the graph-loop advance.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (w == 0) r = warp_sum(r);
+  if (threadIdx.x == 0) red[0] = r;
+  __syncthreads();
+  return red[0];
+}
+
+__device__ __forceinline__ float block_reduce_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (w == 0) r = warp_max(r);
+  if (threadIdx.x == 0) red[0] = r;
+  __syncthreads();
+  return red[0];
+}
+
+// One CTA per weight row. Restates quantized.py:30-39 bit-exactly:
+// max|w| is exact in any order, the divisions are IEEE (__fdiv_rn), rintf rounds half to even.
+__global__ void quantize_rows_kernel(const float* __restrict__ w, int64_t k, int8_t* __restrict__ q,
+                                     float* __restrict__ scales) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float* wr = w + row * k;
+  float mx = 0.f;
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) mx = fmaxf(mx, fabsf(wr[i]));
+  mx = block_reduce_max(mx, red);
+  const float s = fmaxf(__fdiv_rn(mx, 127.0f), 1e-8f);
+  if (threadIdx.x == 0) scales[row] = s;
+  int8_t* qr = q + row * k;
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+    float v = rintf(__fdiv_rn(wr[i], s));
+    v = fminf(fmaxf(v, -128.f), 127.f);
+    qr[i] = static_cast<int8_t>(static_cast<int>(v));
+  }
+}
+
+__global__ void rmsnorm_kernel(const float* __restrict__ h, const float* __restrict__ w, int n, float eps,
+                               __nv_bfloat16* __restrict__ x) {
+  __shared__ float red[32];
+  const float* hr = h + (int64_t)blockIdx.x * n;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += hr[i] * hr[i];
+  ss = block_reduce_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)n + eps);
+  __nv_bfloat16* xr = x + (int64_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __float2bfloat16_rn(w[i] * (hr[i] * inv));
+}
+
+__global__ void layernorm_kernel(const float* __restrict__ h, const float* __restrict__ w,
+                                 const float* __restrict__ b, int n, float eps, __nv_bfloat16* __restrict__ x) {
+  __shared__ float red[32];
+  const float* hr = h + (int64_t)blockIdx.x * n;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += hr[i];
+  const float mean = block_reduce_sum(s, red) / (float)n;
+  float v = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float d = hr[i] - mean;
+    v += d * d;
+  }
+  const float inv = rsqrtf(block_reduce_sum(v, red) / (float)n + eps);
+  __nv_bfloat16* xr = x + (int64_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __float2bfloat16_rn((hr[i] - mean) * inv * w[i] + b[i]);
+}
+
+__global__ void embed_kernel(const int32_t* __restrict__ tokens, const int32_t* __restrict__ positions,
+                             const float* __restrict__ wte, const float* __restrict__ wpe, int hidden, int64_t vocab,
+                             int max_pos, float* __restrict__ h) {
+  const int i = blockIdx.x;
+  const int tok = tokens[i];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 100);
+    return;
+  }
+  int pos = 0;
+  if (wpe) {
+    pos = positions[i];
+    if (pos < 0 || pos >= max_pos) {
+      if (threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 101);
+      return;
+    }
+  }
+  const float* e = wte + (int64_t)tok * hidden;
+  float* hr = h + (int64_t)i * hidden;
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x) hr[j] = e[j] + (wpe ? wpe[(int64_t)pos * hidden + j] : 0.f);
+}
+
+// One CTA per token. Heads [0,hq) are queries, [hq,hq+hkv) keys, [hq+hkv, hq+2hkv) values.
+// Rotate-half RoPE (HF apply_rotary_pos_emb) on q and k; k and v land in the token's paged slot.
+__global__ void rope_kv_append_kernel(const float* __restrict__ qkv, int64_t ld_qkv,
+                                      const int32_t* __restrict__ positions, const float* __restrict__ cos_sin,
+                                      int max_pos, const int32_t* __restrict__ slots, int hq, int hkv, int d,
+                                      float* __restrict__ q_out, __nv_bfloat16* __restrict__ k_pool,
+                                      __nv_bfloat16* __restrict__ v_pool, int64_t num_blocks) {
+  const int i = blockIdx.x;
+  const int half = d >> 1;
+  const float* row = qkv + (int64_t)i * ld_qkv;
+  const float* cs = nullptr;
+  if (cos_sin) {
+    const int pos = positions[i];
+    if (pos < 0 || pos >= max_pos) {
+      if (threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 200);
+      return;
+    }
+    cs = cos_sin + (int64_t)pos * d;
+  }
+  const int slot = slots[i];
+  const int64_t blk = slot >> 4;
+  const int off = slot & 15;
+  const bool slot_ok = slot >= 0 && blk < num_blocks;
+  if (!slot_ok && threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 201);
+  const int nheads = hq + 2 * hkv;
+  for (int e = threadIdx.x; e < nheads * half; e += blockDim.x) {
+    const int hd = e / half, j = e % half;
+    const float* src = row + (int64_t)hd * d;
+    float a = src[j], b = src[j + half];
+    if (hd < hq + hkv && cs) {
+      const float c = cs[j], s = cs[half + j];
+      const float ra = a * c - b * s;
+      const float rb = b * c + a * s;
+      a = ra;
+      b = rb;
+    }
+    if (hd < hq) {
+      float* dst = q_out + ((int64_t)i * hq + hd) * d;
+      dst[j] = a;
+      dst[j + half] = b;
+    } else if (slot_ok) {
+      const bool is_k = hd < hq + hkv;
+      const int kh = is_k ? hd - hq : hd - hq - hkv;
+      __nv_bfloat16* pool = is_k ? k_pool : v_pool;
+      __nv_bfloat16* dst = pool + ((blk * hkv + kh) * 16 + off) * (int64_t)d;
+      dst[j] = __float2bfloat16_rn(a);
+      dst[j + half] = __float2bfloat16_rn(b);
+    }
+  }
+}
+
+// torch.argmax semantics: the first index holding the maximum.
+__global__ void argmax_kernel(const float* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int32_t si[32];
+  const float* r = logits + (int64_t)blockIdx.x * ld;
+  float best = -INFINITY;
+  int32_t bi = 0x7fffffff;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = r[i];
+    if (v > best) {
+      best = v;
+      bi = (int32_t)i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = l < nw ? sv[l] : -INFINITY;
+    bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (l == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+__global__ void decode_advance_kernel(int32_t* tokens, const int32_t* next_tokens, int32_t* positions,
+                                      int32_t* ctx_lens, int32_t* slots, const int32_t* tables, int max_blocks,
+                                      int b) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= b) return;
+  tokens[i] = next_tokens[i];
+  const int pos = positions[i] + 1;
+  positions[i] = pos;
+  ctx_lens[i] = pos + 1;
+  const int lb = pos >> 4;
+  if (lb >= max_blocks) {
+    mg_record_error(MG_ERR_DEVICE, 300);
+    slots[i] = -1;
+    return;
+  }
+  slots[i] = tables[(int64_t)i * max_blocks + lb] * 16 + (pos & 15);
+}
+
+}  // namespace
+
+extern "C" int mg_quantize_rows_i8(const float* w, int64_t n, int64_t k, int8_t* q, float* scales, void* stream) {
+  if (n < 0 || k < 0 || (n > 0 && (!w || !q || !scales)) || n > 0x7fffffff) return MG_ERR_INVALID_ARG;
+  if (n == 0) return MG_OK;
+  quantize_rows_kernel<<<(unsigned)n, kRowThreads, 0, mg_stream(stream)>>>(w, k, q, scales);
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_rmsnorm(const float* h, const float* w, int m, int n, float eps, void* x, void* stream) {
+  if (m < 0 || n <= 0 || !h || !w || !x) return MG_ERR_INVALID_ARG;
+  if (m == 0) return MG_OK;
+  rmsnorm_kernel<<<m, kRowThreads, 0, mg_stream(stream)>>>(h, w, n, eps, static_cast<__nv_bfloat16*>(x));
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_layernorm(const float* h, const float* w, const float* bias, int m, int n, float eps, void* x,
+                            void* stream) {
+  if (m < 0 || n <= 0 || !h || !w || !bias || !x) return MG_ERR_INVALID_ARG;
+  if (m == 0) return MG_OK;
+  layernorm_kernel<<<m, kRowThreads, 0, mg_stream(stream)>>>(h, w, bias, n, eps, static_cast<__nv_bfloat16*>(x));
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_embed(const int32_t* tokens, const int32_t* positions, const float* wte, const float* wpe, int b,
+                        int hidden, int64_t vocab, int max_pos, float* h, void* stream) {
+  if (b < 0 || hidden <= 0 || vocab <= 0 || !tokens || !wte || !h || (wpe && (!positions || max_pos <= 0)))
+    return MG_ERR_INVALID_ARG;
+  if (b == 0) return MG_OK;
+  embed_kernel<<<b, kRowThreads, 0, mg_stream(stream)>>>(tokens, positions, wte, wpe, hidden, vocab, max_pos, h);
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t* positions, const float* cos_sin,
+                                 int max_pos, const int32_t* slot_mapping, int b, int hq, int hkv, int d,
+                                 float* q_out, void* k_pool, void* v_pool, int64_t num_blocks, void* stream) {
+  if (b < 0 || hq <= 0 || hkv <= 0 || hq % hkv || d <= 0 || (d & 1) || !qkv || !slot_mapping || !q_out || !k_pool ||
+      !v_pool || num_blocks <= 0 || ld_qkv < (int64_t)(hq + 2 * hkv) * d || (cos_sin && (!positions || max_pos <= 0)))
+    return MG_ERR_INVALID_ARG;
+  if (b == 0) return MG_OK;
+  rope_kv_append_kernel<<<b, kRowThreads, 0, mg_stream(stream)>>>(
+      qkv, ld_qkv, positions, cos_sin, max_pos, slot_mapping, hq, hkv, d, q_out,
+      static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), num_blocks);
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_argmax_rows(const float* logits, int m, int64_t n, int64_t ld, int32_t* out, void* stream) {
+  if (m < 0 || n <= 0 || ld < n || !logits || !out || n > 0x7fffffff) return MG_ERR_INVALID_ARG;
+  if (m == 0) return MG_OK;
+  argmax_kernel<<<m, 1024, 0, mg_stream(stream)>>>(logits, n, ld, out);
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_decode_advance(int32_t* tokens, const int32_t* next_tokens, int32_t* positions, int32_t* ctx_lens,
+                                 int32_t* slots, const int32_t* block_tables, int max_blocks, int b, void* stream) {
+  if (b < 0 || max_blocks <= 0 || !tokens || !next_tokens || !positions || !ctx_lens || !slots || !block_tables)
+    return MG_ERR_INVALID_ARG;
+  if (b == 0) return MG_OK;
+  decode_advance_kernel<<<(b + 127) / 128, 128, 0, mg_stream(stream)>>>(tokens, next_tokens, positions, ctx_lens,
+                                                                        slots, block_tables, max_blocks, b);
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}

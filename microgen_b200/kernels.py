@@ -1,0 +1,175 @@
+"""Torch-tensor wrappers over the C ABI (device memory and streams come from torch).
+
+Each wrapper checks dtypes, devices and layout, then launches the kernel on the
+current CUDA stream. Tensors must live on a CUDA device; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import (EPI_ADD_F32, EPI_GELU_BF16, EPI_STORE_BF16, EPI_STORE_F32,  # noqa: F401
+                   EPI_SWIGLU_BF16)
+
+BLOCK_SIZE = 16
+
+
+def _ptr(t: torch.Tensor | None) -> C.c_void_p:
+    return C.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream() -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str, contiguous: bool = True) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the decode path has no CPU fallback)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def quantize_rows_i8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(codes int8 [N,K], scales fp32 [N]) of an fp32 weight, bit-exact with the reference."""
+    _need(w, torch.float32, "w")
+    n, k = w.shape
+    q = torch.empty((n, k), dtype=torch.int8, device=w.device)
+    s = torch.empty((n,), dtype=torch.float32, device=w.device)
+    _lib.call("mg_quantize_rows_i8", _ptr(w), n, k, _ptr(q), _ptr(s), _stream())
+    return q, s
+
+
+def _linear_args(x, q, scales, bias, y, epilogue):
+    _need(q, torch.int8, "q")
+    _need(scales, torch.float32, "scales")
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+    _need(x, torch.bfloat16, "x", contiguous=False)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be 2-D with unit inner stride")
+    n, k = q.shape
+    if x.shape[1] != k:
+        raise ValueError(f"x has {x.shape[1]} features, weight expects {k}")
+    m = x.shape[0]
+    if y is None:
+        nout = n // 2 if epilogue == EPI_SWIGLU_BF16 else n
+        dt = torch.float32 if epilogue in (EPI_STORE_F32, EPI_ADD_F32) else torch.bfloat16
+        y = torch.empty((m, nout), dtype=dt, device=x.device)
+    want = torch.float32 if epilogue in (EPI_STORE_F32, EPI_ADD_F32) else torch.bfloat16
+    _need(y, want, "y", contiguous=False)
+    if y.dim() != 2 or y.stride(1) != 1 or y.shape[0] != m:
+        raise ValueError("y must be [m, n] with unit inner stride")
+    return m, k, n, y
+
+
+def i8_linear(x, q, scales, bias=None, y=None, epilogue=EPI_STORE_BF16, algo: str = "auto", split_k: int = 0):
+    """y = epilogue(x · (q·s)ᵀ + bias); returns y. algo: "auto" | "tc" | "simt"."""
+    m, k, n, y = _linear_args(x, q, scales, bias, y, epilogue)
+    args = (_ptr(x), m, k, x.stride(0), _ptr(q), _ptr(scales), _ptr(bias), n, _ptr(y), y.stride(0), int(epilogue))
+    if algo == "simt":
+        _lib.call("mg_i8_linear_simt", *args, _stream())
+    elif algo == "tc":
+        _lib.call("mg_i8_linear_tc", *args, int(split_k), _stream())
+    else:
+        _lib.call("mg_i8_linear", *args, _stream())
+    return y
+
+
+def rope_kv_append(qkv, positions, cos_sin, slots, hq, hkv, d, k_pool, v_pool, q_out=None):
+    _need(qkv, torch.float32, "qkv", contiguous=False)
+    _need(slots, torch.int32, "slots")
+    _need(k_pool, torch.bfloat16, "k_pool")
+    _need(v_pool, torch.bfloat16, "v_pool")
+    b = qkv.shape[0]
+    if cos_sin is not None:
+        _need(cos_sin, torch.float32, "cos_sin")
+        _need(positions, torch.int32, "positions")
+    if q_out is None:
+        q_out = torch.empty((b, hq, d), dtype=torch.float32, device=qkv.device)
+    _lib.call("mg_rope_kv_append", _ptr(qkv), qkv.stride(0), _ptr(positions), _ptr(cos_sin),
+              0 if cos_sin is None else cos_sin.shape[0], _ptr(slots), b, hq, hkv, d, _ptr(q_out), _ptr(k_pool),
+              _ptr(v_pool), k_pool.shape[0], _stream())
+    return q_out
+
+
+def attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks=0) -> int:
+    out = C.c_size_t(0)
+    _lib.call("mg_paged_attn_workspace_bytes", b, hq, hkv, d, max_blocks, n_shared_blocks, C.byref(out))
+    return out.value
+
+
+def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared_blocks=0, out=None,
+                      workspace=None):
+    """q fp32 [b, hq, d]; pools bf16 [nblk, hkv, 16, d]; tables int32 [b, max_blocks]; ctx int32 [b].
+    Returns bf16 [b, hq*d]."""
+    _need(q, torch.float32, "q")
+    _need(k_pool, torch.bfloat16, "k_pool")
+    _need(v_pool, torch.bfloat16, "v_pool")
+    _need(block_tables, torch.int32, "block_tables")
+    _need(ctx_lens, torch.int32, "ctx_lens")
+    b, hq, d = q.shape
+    hkv = k_pool.shape[1]
+    max_blocks = block_tables.shape[1]
+    ws = attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks)
+    if ws and (workspace is None or workspace.numel() * workspace.element_size() < ws):
+        workspace = torch.empty(ws, dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty((b, hq * d), dtype=torch.bfloat16, device=q.device)
+    _lib.call("mg_paged_decode_attn", _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables),
+              max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks, float(scale), _ptr(out),
+              _ptr(workspace if ws else None), ws, _stream())
+    return out
+
+
+def embed(tokens, positions, wte, wpe, h):
+    _need(tokens, torch.int32, "tokens")
+    _need(wte, torch.float32, "wte")
+    _need(h, torch.float32, "h")
+    max_pos = 0
+    if wpe is not None:
+        _need(wpe, torch.float32, "wpe")
+        _need(positions, torch.int32, "positions")
+        max_pos = wpe.shape[0]
+    _lib.call("mg_embed", _ptr(tokens), _ptr(positions), _ptr(wte), _ptr(wpe), tokens.shape[0], wte.shape[1],
+              wte.shape[0], max_pos, _ptr(h), _stream())
+    return h
+
+
+def rmsnorm(h, w, eps, x=None):
+    _need(h, torch.float32, "h")
+    _need(w, torch.float32, "w")
+    if x is None:
+        x = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device)
+    _lib.call("mg_rmsnorm", _ptr(h), _ptr(w), h.shape[0], h.shape[1], float(eps), _ptr(x), _stream())
+    return x
+
+
+def layernorm(h, w, b, eps, x=None):
+    _need(h, torch.float32, "h")
+    if x is None:
+        x = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device)
+    _lib.call("mg_layernorm", _ptr(h), _ptr(w), _ptr(b), h.shape[0], h.shape[1], float(eps), _ptr(x), _stream())
+    return x
+
+
+def argmax_rows(logits, out=None):
+    _need(logits, torch.float32, "logits", contiguous=False)
+    if out is None:
+        out = torch.empty((logits.shape[0],), dtype=torch.int32, device=logits.device)
+    _lib.call("mg_argmax_rows", _ptr(logits), logits.shape[0], logits.shape[1], logits.stride(0), _ptr(out),
+              _stream())
+    return out
+
+
+def decode_advance(tokens, next_tokens, positions, ctx_lens, slots, block_tables):
+    _lib.call("mg_decode_advance", _ptr(tokens), _ptr(next_tokens), _ptr(positions), _ptr(ctx_lens), _ptr(slots),
+              _ptr(block_tables), block_tables.shape[1], tokens.shape[0], _stream())
+
+
+def check_device() -> None:
+    _lib.check_device(torch.cuda.current_stream().cuda_stream)
