@@ -1,0 +1,352 @@
+"""Decode-step benchmark: INT8 tensor-parallel linears + paged decode attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload llama3b|qwen05b|gpt2]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...   (N > 1, TP = N)
+    python bench.py --impl reference ...   (the reference's CPU path, restated as the oracle port)
+
+Workload (default): Llama-3.2-3B-shaped decoder (28 layers, hidden 3072, 24/8 heads of 128,
+SwiGLU 8192, vocab 128256), random-init N(0, 0.02) weights quantized to INT8 per output
+channel, batch 32, prompts of 2048 uniform random ids whose first 1024 are shared (prefilled
+once, blocks shared by reference count), block tables from a seeded shuffled free list,
+then greedy decode. A step is one decode step of the whole batch (all layers, lm_head,
+argmax). ``value`` = batch / device time per step (tokens/s), timed with CUDA events over K
+CUDA-graph replays whose mean context equals the decode phase's mean (2048 + 256); the
+per-step working set (3.2 GB of weights + 4.8 GB of KV) is far larger than L2, so no flush
+is needed. ``e2e`` is the same decode through the backend's public API (host token ids in,
+greedy ids out) with the host<->device copies inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "llama3b": dict(shape="LLAMA_3B", batch=32, prompt=2048, shared=1024, decode=512),
+    "qwen05b": dict(shape="QWEN_05B", batch=16, prompt=1024, shared=0, decode=256),
+    "gpt2": dict(shape="GPT2_SMALL", batch=8, prompt=512, shared=0, decode=256),
+}
+METRIC = "decode tokens/s at 1/2/4/8 B200; INT8 TP-linear HBM GB/s vs roofline"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="llama3b", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (debug)")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid, self.proc, self.path = uuid, None, None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+            if self.uuid:
+                cmd += ["-i", self.uuid]
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def cpu_baseline(spec, wl, ctx, budget_s=20.0) -> dict:
+    from oracle.cpu_baseline import measure
+    r = measure(spec.hidden, spec.heads, spec.kv_heads, spec.head_dim, spec.inter, spec.vocab, spec.layers,
+                wl["batch"], ctx, budget_s=budget_s, eps=spec.eps, theta=spec.rope_theta)
+    return {"value": round(r["tokens_per_s"], 4), "unit": "tokens/s", "cores": r["threads"], "kind": "port",
+            "sample": (f"numpy fp32 restatement of the reference CPU decode step (dequantize-per-call linears, "
+                       f"cat-grown cache, SDPA) at the full {wl['shape']} shape, batch {wl['batch']}, ctx {ctx}: "
+                       f"{r['layers_timed']} single-layer steps timed ({r['layer_s']:.3f} s each) + lm_head "
+                       f"({r['head_s']:.3f} s); step = {spec.layers} x layer + head = {r['step_s']:.2f} s")}
+
+
+def run_reference(args) -> None:
+    """The reference arm: the reference path is Python on the host CPU; it cannot be installed
+    on the GPU box, so its restatement (the oracle port) is timed on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from microgen_b200.model_spec import ModelSpec, GPT2_SMALL, LLAMA_3B, QWEN_05B  # noqa: F401
+    wl = WORKLOADS[args.workload]
+    spec = ModelSpec(**globals()[wl["shape"]] if wl["shape"] in globals() else
+                     {"LLAMA_3B": LLAMA_3B, "QWEN_05B": QWEN_05B, "GPT2_SMALL": GPT2_SMALL}[wl["shape"]])
+    ctx = wl["prompt"] + wl["decode"] // 2
+    budget = min(90.0, max(10.0, 2.0 * (args.steps + args.warmup)))
+    cb = cpu_baseline(spec, wl, ctx, budget_s=budget)
+    v = cb["value"]
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * wl["batch"] / v, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {wl}", "tp": 1, "device": "host cpu"},
+        "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from microgen_b200 import _lib
+    from microgen_b200 import kernels as K
+    from microgen_b200 import model_spec as MS
+    from microgen_b200.backends import B200QuantizedBackend, B200TensorParallelBackend
+    from microgen_b200.synthetic import SyntheticState
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+
+    wl = dict(WORKLOADS[args.workload])
+    if args.prompt:
+        wl["prompt"], wl["shared"] = args.prompt, min(wl["shared"], args.prompt // 2)
+    spec = MS.ModelSpec(**getattr(MS, wl["shape"]))
+    B, P, S, Dec = wl["batch"], wl["prompt"], wl["shared"], wl["decode"]
+    W, Kst = args.warmup, args.steps
+    skip = max(0, Dec // 2 - W - Kst // 2)
+    run = skip + W + Kst
+    max_seq = P + max(Dec, run) + 16
+    max_blocks = (max_seq + 15) // 16
+    n_shared = S // 16
+    num_blocks = n_shared + B * (max_blocks - n_shared) + 16
+
+    kw = dict(max_batch=B, max_seq_len=max_seq, num_blocks=num_blocks, free_list_seed=0)
+    be = (B200TensorParallelBackend(world_size=world, group=group, **kw) if world > 1
+          else B200QuantizedBackend(**kw))
+    t0 = time.time()
+    be.load_state(spec, SyntheticState(spec, seed=0, device=torch.device("cuda", local)))
+    torch.cuda.synchronize()
+    t_load = time.time() - t0
+    eng = be.engine
+
+    g = torch.Generator().manual_seed(1)
+    shared = torch.randint(0, spec.vocab, (S,), generator=g)
+    prompts = torch.stack([torch.cat([shared, torch.randint(0, spec.vocab, (P - S,), generator=g)])
+                           for _ in range(B)])
+    t0 = time.time()
+    logits, cache = be.prefill(prompts)
+    torch.cuda.synchronize()
+    t_prefill = time.time() - t0
+    first = be.sample(logits)[:, 0].to(torch.int32).cpu()
+
+    # ---- device-timed decode: graph replays, inputs resident, device-side advance --------------
+    alloc = be.allocator
+    for t in cache.tables:
+        for _ in range(run + 1):
+            alloc.append_token(t)
+    from microgen_b200.runtime.paged_kv import block_table_tensor
+    tab = block_table_tensor(cache.tables, eng.max_blocks)
+    slots = [t.slot(P) for t in cache.tables]
+    eng.set_inputs(first.tolist(), [P] * B, slots, [P + 1] * B, tab)
+    before = _lib.LAUNCHES[0]
+    graph = eng.capture(B, cache.n_shared_blocks, advance=True)
+    per_step_launches = _lib.LAUNCHES[0] - before
+    # capture() ran one warm-up step (not advanced); the launch count of capture = warm-up + graph
+    per_step_launches //= 2
+    for _ in range(skip + W):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+        pass
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(uuid) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(Kst):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / Kst
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = B / (ms / 1e3)
+    mean_pos = P + skip + W + (Kst - 1) / 2.0
+    kv_tokens = n_shared * 16 + B * (int(mean_pos) + 1 - n_shared * 16)
+
+    # ---- per-kernel device time (probe pass, eager, CUDA events on the launch stream) ----------
+    stats: dict = {}
+
+    class Probe:
+        def __init__(self, kind, nbytes):
+            self.kind, self.nbytes = kind, nbytes
+
+        def __enter__(self):
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.b = torch.cuda.Event(enable_timing=True)
+            self.a.record(torch.cuda.current_stream())
+
+        def __exit__(self, *e):
+            self.b.record(torch.cuda.current_stream())
+            stats.setdefault(self.kind, []).append((self.a, self.b, self.nbytes))
+
+    pos = int(mean_pos)
+    eng.set_inputs(first.tolist(), [pos] * B, [t.slot(pos) for t in cache.tables], [pos + 1] * B, tab)
+    for rep in range(4):
+        if rep == 1:
+            stats.clear()
+        eng.forward(B, cache.n_shared_blocks, probe=Probe, kv_tokens=kv_tokens)
+    torch.cuda.synchronize()
+    kernels = {}
+    for kind, recs in stats.items():
+        tsum = sum(a.elapsed_time(b) for a, b, _ in recs) / 1e3
+        bsum = sum(n for _, _, n in recs)
+        kernels[kind] = {"launches_per_step": len(recs) // 3, "us_per_step": round(tsum / 3 * 1e6, 2),
+                         "gbs": round(bsum / tsum / 1e9, 1)}
+    hbm, hbm_kind = peaks()
+    dom = max(("paged_attn", "i8_linear"), key=lambda k: kernels.get(k, {}).get("us_per_step", 0.0))
+    recs = stats[dom]
+    t_dom = sum(a.elapsed_time(b) for a, b, _ in recs) / 1e3
+    achieved = sum(n for _, _, n in recs) / t_dom / 1e9
+    traffic = None
+    tr_path = os.path.join(ROOT, "profiles", "traffic_per_launch.json")
+    if os.path.exists(tr_path):
+        try:
+            traffic = json.load(open(tr_path)).get(f"{args.workload}:{dom}")
+        except Exception:
+            traffic = None
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": hbm_kind}
+    step_bytes = eng.w.int8_bytes() + kv_tokens * eng.hkv * spec.head_dim * 2 * 2 * spec.layers
+    step_roofline = {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms / 1e3) / 1e9, 1),
+                     "frac": round(step_bytes / (ms / 1e3) / 1e9 / hbm, 4)}
+
+    # ---- end to end through the public API (host ids in, host ids out) -------------------------
+    e2e = None
+    if not args.no_e2e:
+        for t in cache.tables:
+            alloc.rollback(t, t.num_tokens - (P + skip))
+        tok = first[:, None].to(torch.int64)
+        for _ in range(W):
+            lg, cache = be.decode(tok, cache=cache)
+            tok = be.sample(lg).cpu()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(Kst):
+            lg, cache = be.decode(tok, cache=cache)
+            tok = be.sample(lg).cpu()
+        f1.record()
+        torch.cuda.synchronize()
+        ems = f0.elapsed_time(f1) / Kst
+        if world > 1:
+            t = torch.tensor([ems], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": round(B / (ems / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": eng.h2d_bytes,
+               "d2h_bytes_per_step": B * 8, "ms_per_step": round(ems, 4)}
+    K.check_device()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(spec, wl, P + Dec // 2, budget_s=20.0)
+
+    eng.release_graphs()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": Kst,
+        "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 weights x bf16 activations, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {wl['shape']} INT8, batch {B}, prompt {P} ({S} shared), decode "
+                               f"{Dec}; timed window mean ctx {mean_pos + 1:.0f}",
+                   "batch": B, "prompt": P, "shared_prefix": S, "tp": world, "parallelism": f"tp{world}",
+                   "l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True},
+        "roofline": roofline, "step_roofline": step_roofline, "kernels": kernels,
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst,
+        "clocks": clk.summary(), "setup_s": {"load": round(t_load, 1), "prefill": round(t_prefill, 1)},
+    }
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

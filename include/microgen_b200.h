@@ -83,7 +83,7 @@ int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t* positions
 /* ---- paged decode attention ---------------------------------------------------------------- */
 /* out bf16 [b, hq*d] = softmax(q·Kᵀ·scale)·V per sequence, query head h reading kv head
  * h / (hq/hkv); K/V gathered through block_tables int32 [b, max_blocks] from pools
- * bf16 [num_blocks, hkv, 16, d]; ctx_lens int32 [b] >= 1. d in {64, 128}; hq/hkv <= 16.
+ * bf16 [num_blocks, hkv, 16, d]; ctx_lens int32 [b] >= 1. d in {32, 64, 128}; hq/hkv <= 16.
  * n_shared_blocks: the first n_shared_blocks entries of every table are the same blocks
  * (a shared prefix); they are read once per batch. 0 = no sharing.
  * workspace: device scratch of mg_paged_attn_workspace_bytes() bytes (may be NULL if 0). */

@@ -48,6 +48,12 @@ SIGNATURES = {
 }
 _RESTYPES = {"mg_status_string": C.c_char_p}
 
+# entry points that launch one kernel per call (mg_paged_decode_attn adds its combine kernel)
+LAUNCHING = {"mg_quantize_rows_i8", "mg_i8_linear", "mg_i8_linear_simt", "mg_i8_linear_tc", "mg_rope_kv_append",
+             "mg_paged_decode_attn", "mg_embed", "mg_rmsnorm", "mg_layernorm", "mg_argmax_rows",
+             "mg_decode_advance"}
+LAUNCHES = [0]  # kernels launched (or captured) through call() in this process
+
 _lock = threading.Lock()
 _lib = None
 
@@ -88,6 +94,8 @@ def status_string(status: int) -> str:
 def call(name: str, *args) -> None:
     """Call an entry point; raise MGError (TimeoutError for MG_ERR_TIMEOUT) on a nonzero status."""
     rc = getattr(load(), name)(*args)
+    if rc == MG_OK and name in LAUNCHING:
+        LAUNCHES[0] += 1
     if rc != MG_OK:
         detail = ""
         if rc == MG_ERR_CUDA:

@@ -432,7 +432,7 @@ extern "C" int mg_paged_attn_workspace_bytes(int b, int hq, int hkv, int d, int 
   if (!bytes || b < 0 || hq <= 0 || hkv <= 0 || hq % hkv || max_blocks <= 0 || n_shared_blocks < 0 ||
       n_shared_blocks > max_blocks)
     return MG_ERR_INVALID_ARG;
-  if (d != 64 && d != 128) return MG_ERR_UNSUPPORTED;
+  if (d != 32 && d != 64 && d != 128) return MG_ERR_UNSUPPORTED;
   *bytes = make_plan(b, hq, hkv, d, max_blocks, n_shared_blocks).ws_bytes;
   return MG_OK;
 }
@@ -445,7 +445,7 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
       n_shared_blocks < 0 || n_shared_blocks > max_blocks || !q || !k_pool || !v_pool || !block_tables ||
       !ctx_lens || !out)
     return MG_ERR_INVALID_ARG;
-  if (d != 64 && d != 128) return MG_ERR_UNSUPPORTED;
+  if (d != 32 && d != 64 && d != 128) return MG_ERR_UNSUPPORTED;
   if (b == 0) return MG_OK;
   const Plan pl = make_plan(b, hq, hkv, d, max_blocks, n_shared_blocks);
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes)) return MG_ERR_INVALID_ARG;
@@ -474,5 +474,6 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
   p.ws_ml = pl.ws_bytes ? static_cast<float*>(workspace) + (size_t)b * hq * pl.nslots * d : nullptr;
   p.direct = pl.direct;
   cudaStream_t st = mg_stream(stream);
+  if (d == 32) return launch_attn<32>(p, pl, st);
   return d == 64 ? launch_attn<64>(p, pl, st) : launch_attn<128>(p, pl, st);
 }

@@ -1,0 +1,359 @@
+"""Decode engine: one decode step of a Llama / Qwen2 / GPT-2 model as a sequence of
+libmicrogen_b200 kernel launches over device-resident INT8 weights and a paged KV pool.
+
+This is what runs inside ``backend.decode`` (``microgen/backends/pytorch.py:118-142``)
+once the backend has swapped in the INT8 tensor-parallel linears:
+
+    embed → per layer: norm → QKV (column-parallel INT8 linear) → RoPE + paged KV
+    append → paged decode attention → o_proj (row-parallel INT8 linear, residual
+    add, all-reduce) → norm → gate/up with fused SwiGLU (or c_fc with GELU) →
+    down (row-parallel, residual add, all-reduce) → final norm → lm_head → argmax
+
+Weights are quantized on the device with the bit-exact per-channel kernel from the
+FULL fp32 matrices, then sharded (column: rows and scales split per head group;
+row: input columns split, scales replicated), so codes at TP=N equal codes at TP=1.
+The residual stream stays fp32; activations entering a linear are bf16; K/V are bf16.
+
+Row-parallel linears reduce with the "store-or-add" trick: rank 0 adds its partial
+(and the bias) into the residual in place, the other ranks overwrite their copy
+with their partial, and one in-place sum all-reduce of the residual completes
+``h + Σ partials`` — no extra kernel on the path.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from . import kernels as K
+from .model_spec import ModelSpec
+from .runtime.paged_kv import PagedKVPool
+
+
+@dataclass
+class LayerWeights:
+    ln1_w: torch.Tensor
+    ln1_b: Optional[torch.Tensor]
+    qkv_q: torch.Tensor
+    qkv_s: torch.Tensor
+    qkv_b: Optional[torch.Tensor]
+    o_q: torch.Tensor
+    o_s: torch.Tensor
+    o_b: Optional[torch.Tensor]
+    ln2_w: torch.Tensor
+    ln2_b: Optional[torch.Tensor]
+    gu_q: torch.Tensor
+    gu_s: torch.Tensor
+    gu_b: Optional[torch.Tensor]
+    d_q: torch.Tensor
+    d_s: torch.Tensor
+    d_b: Optional[torch.Tensor]
+
+
+@dataclass
+class ModelWeights:
+    embed: torch.Tensor
+    wpe: Optional[torch.Tensor]
+    norm_w: torch.Tensor
+    norm_b: Optional[torch.Tensor]
+    lm_q: torch.Tensor
+    lm_s: torch.Tensor
+    layers: list = field(default_factory=list)
+
+    def nbytes(self) -> int:
+        n = 0
+        for t in [self.embed, self.wpe, self.norm_w, self.norm_b, self.lm_q, self.lm_s]:
+            n += 0 if t is None else t.numel() * t.element_size()
+        for L in self.layers:
+            for t in vars(L).values():
+                n += 0 if t is None else t.numel() * t.element_size()
+        return n
+
+    def int8_bytes(self) -> int:
+        """Weight bytes a decode step streams: int8 codes + fp32 scales of every linear."""
+        n = self.lm_q.numel() + 4 * self.lm_s.numel()
+        for L in self.layers:
+            for q, s in ((L.qkv_q, L.qkv_s), (L.o_q, L.o_s), (L.gu_q, L.gu_s), (L.d_q, L.d_s)):
+                n += q.numel() + 4 * s.numel()
+        return n
+
+
+def _interleave_gate_up(gq, gs, uq, us, gb=None, ub=None):
+    """Rows grouped as [64 gate rows, the 64 matching up rows] per 128 (the SwiGLU epilogue layout)."""
+    i, k = gq.shape
+    if i % 64:
+        raise ValueError(f"intermediate size per rank ({i}) must be a multiple of 64")
+    q = torch.stack([gq.view(i // 64, 64, k), uq.view(i // 64, 64, k)], dim=1).reshape(2 * i, k).contiguous()
+    s = torch.stack([gs.view(i // 64, 64), us.view(i // 64, 64)], dim=1).reshape(2 * i).contiguous()
+    b = None
+    if gb is not None or ub is not None:
+        gb = gb if gb is not None else torch.zeros_like(gs)
+        ub = ub if ub is not None else torch.zeros_like(us)
+        b = torch.stack([gb.view(i // 64, 64), ub.view(i // 64, 64)], dim=1).reshape(2 * i).contiguous()
+    return q, s, b
+
+
+class WeightLoader:
+    """Quantize full fp32 matrices on the device and keep this rank's shard."""
+
+    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1):
+        self.spec, self.device, self.rank, self.world = spec, torch.device(device), rank, world
+        if spec.heads % world or spec.kv_heads % world:
+            raise ValueError(f"{spec.heads} query / {spec.kv_heads} kv heads do not split over {world} ranks")
+
+    def f32(self, t) -> torch.Tensor:
+        return t.detach().to(device=self.device, dtype=torch.float32).contiguous()
+
+    def quant(self, w_out_in) -> tuple[torch.Tensor, torch.Tensor]:
+        return K.quantize_rows_i8(self.f32(w_out_in))
+
+    def rows(self, t, n_total):
+        per = n_total // self.world
+        return t[self.rank * per:(self.rank + 1) * per].contiguous()
+
+    def cols(self, q, k_total):
+        per = k_total // self.world
+        return q[:, self.rank * per:(self.rank + 1) * per].contiguous()
+
+    def bias(self, b):
+        return None if b is None else self.f32(b)
+
+    def load(self, state: dict) -> ModelWeights:
+        s = self.spec
+        D = s.head_dim
+        qn, kn = s.heads * D, s.kv_heads * D
+        g = lambda k: state[k] if k in state else None
+        layers = []
+        gpt2 = s.family == "gpt2"
+        for i in range(s.layers):
+            if gpt2:
+                p = f"transformer.h.{i}."
+                wqkv = g(p + "attn.c_attn.weight").t()
+                bqkv = g(p + "attn.c_attn.bias")
+                wq, wk, wv = wqkv[:qn], wqkv[qn:qn + kn], wqkv[qn + kn:]
+                bq, bk, bv = (None, None, None) if bqkv is None else (bqkv[:qn], bqkv[qn:qn + kn], bqkv[qn + kn:])
+                wo, bo = g(p + "attn.c_proj.weight").t(), g(p + "attn.c_proj.bias")
+                wfc, bfc = g(p + "mlp.c_fc.weight").t(), g(p + "mlp.c_fc.bias")
+                wd, bd = g(p + "mlp.c_proj.weight").t(), g(p + "mlp.c_proj.bias")
+                ln1 = (g(p + "ln_1.weight"), g(p + "ln_1.bias"))
+                ln2 = (g(p + "ln_2.weight"), g(p + "ln_2.bias"))
+            else:
+                p = f"model.layers.{i}."
+                wq, wk, wv = (g(p + f"self_attn.{n}_proj.weight") for n in "qkv")
+                bq, bk, bv = (g(p + f"self_attn.{n}_proj.bias") for n in "qkv")
+                wo, bo = g(p + "self_attn.o_proj.weight"), g(p + "self_attn.o_proj.bias")
+                wg, wu = g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")
+                bg, bu = g(p + "mlp.gate_proj.bias"), g(p + "mlp.up_proj.bias")
+                wd, bd = g(p + "mlp.down_proj.weight"), g(p + "mlp.down_proj.bias")
+                ln1 = (g(p + "input_layernorm.weight"), None)
+                ln2 = (g(p + "post_attention_layernorm.weight"), None)
+            # column-parallel QKV: each projection quantized whole, then this rank's head rows
+            parts_q, parts_s, parts_b = [], [], []
+            for w_, b_, n_ in ((wq, bq, qn), (wk, bk, kn), (wv, bv, kn)):
+                q_, s_ = self.quant(w_)
+                parts_q.append(self.rows(q_, n_))
+                parts_s.append(self.rows(s_, n_))
+                parts_b.append(self.rows(self.f32(b_), n_) if b_ is not None else None)
+            qkv_b = None
+            if any(b is not None for b in parts_b):
+                qkv_b = torch.cat([b if b is not None else torch.zeros_like(sq) for b, sq in zip(parts_b, parts_s)])
+            # row-parallel o / down: full-matrix scales replicated, input columns split
+            o_q, o_s = self.quant(wo)
+            d_q, d_s = self.quant(wd)
+            if gpt2:
+                fq, fs = self.quant(wfc)
+                gu_q, gu_s = self.rows(fq, s.inter), self.rows(fs, s.inter)
+                gu_b = self.rows(self.f32(bfc), s.inter) if bfc is not None else None
+            else:
+                gq, gs = self.quant(wg)
+                uq, us = self.quant(wu)
+                gu_q, gu_s, gu_b = _interleave_gate_up(
+                    self.rows(gq, s.inter), self.rows(gs, s.inter), self.rows(uq, s.inter), self.rows(us, s.inter),
+                    self.rows(self.f32(bg), s.inter) if bg is not None else None,
+                    self.rows(self.f32(bu), s.inter) if bu is not None else None)
+            layers.append(LayerWeights(
+                ln1_w=self.f32(ln1[0]), ln1_b=self.bias(ln1[1]),
+                qkv_q=torch.cat(parts_q).contiguous(), qkv_s=torch.cat(parts_s).contiguous(), qkv_b=qkv_b,
+                o_q=self.cols(o_q, qn), o_s=o_s, o_b=self.bias(bo) if self.rank == 0 else None,
+                ln2_w=self.f32(ln2[0]), ln2_b=self.bias(ln2[1]),
+                gu_q=gu_q, gu_s=gu_s, gu_b=gu_b,
+                d_q=self.cols(d_q, s.inter), d_s=d_s, d_b=self.bias(bd) if self.rank == 0 else None))
+        if gpt2:
+            embed, wpe = self.f32(state["transformer.wte.weight"]), self.f32(state["transformer.wpe.weight"])
+            norm_w, norm_b = self.f32(state["transformer.ln_f.weight"]), self.f32(state["transformer.ln_f.bias"])
+            head = state.get("lm_head.weight", state["transformer.wte.weight"])
+        else:
+            embed, wpe = self.f32(state["model.embed_tokens.weight"]), None
+            norm_w, norm_b = self.f32(state["model.norm.weight"]), None
+            head = state.get("lm_head.weight", state["model.embed_tokens.weight"])
+        lm_q, lm_s = self.quant(head)
+        return ModelWeights(embed=embed, wpe=wpe, norm_w=norm_w, norm_b=norm_b, lm_q=lm_q, lm_s=lm_s, layers=layers)
+
+
+def rope_table(head_dim: int, theta: float, max_pos: int) -> torch.Tensor:
+    """fp32 [max_pos, head_dim]: cos of the head_dim/2 frequencies, then sin — computed as HF's
+    default rotary embedding does (fp32 inv_freq, fp32 angle, fp32 cos/sin)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(torch.float32) / head_dim))
+    pos = torch.arange(max_pos, dtype=torch.float32)
+    ang = pos[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).contiguous()
+
+
+class DecodeEngine:
+    """Device state of one rank: weights, paged KV pool, step buffers, captured graphs."""
+
+    def __init__(self, spec: ModelSpec, weights: ModelWeights, device, max_batch: int, num_blocks: int,
+                 max_blocks_per_seq: int, rank: int = 0, world: int = 1, group=None, max_pos: int = 0):
+        self.spec, self.w, self.device = spec, weights, torch.device(device)
+        self.rank, self.world, self.group = rank, world, group
+        self.hq, self.hkv, self.D = spec.heads // world, spec.kv_heads // world, spec.head_dim
+        self.inter = spec.inter // world
+        self.max_batch, self.max_blocks = max_batch, max_blocks_per_seq
+        self.max_ctx = max_blocks_per_seq * 16
+        self.pool = PagedKVPool(spec.layers, num_blocks, self.hkv, self.D, self.device)
+        self.scale = 1.0 / math.sqrt(self.D)
+        dev = self.device
+        if spec.family == "gpt2":
+            self.cos_sin = None
+        else:
+            self.cos_sin = rope_table(self.D, spec.rope_theta, max(max_pos, self.max_ctx)).to(dev)
+        B, H = max_batch, spec.hidden
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros(B, **i32)
+        self.positions = torch.zeros(B, **i32)
+        self.slots = torch.zeros(B, **i32)
+        self.ctx = torch.ones(B, **i32)
+        self.tables = torch.zeros((B, max_blocks_per_seq), **i32)
+        self.next_tokens = torch.zeros(B, **i32)
+        self.h = torch.zeros((B, H), dtype=torch.float32, device=dev)
+        self.x = torch.zeros((B, H), dtype=torch.bfloat16, device=dev)
+        self.qkv = torch.zeros((B, (self.hq + 2 * self.hkv) * self.D), dtype=torch.float32, device=dev)
+        self.q = torch.zeros((B, self.hq, self.D), dtype=torch.float32, device=dev)
+        self.attn = torch.zeros((B, self.hq * self.D), dtype=torch.bfloat16, device=dev)
+        self.act = torch.zeros((B, self.inter), dtype=torch.bfloat16, device=dev)
+        self.logits = torch.zeros((B, spec.vocab), dtype=torch.float32, device=dev)
+        ws = max(K.attn_workspace_bytes(b, self.hq, self.hkv, self.D, max_blocks_per_seq, ns)
+                 for b in {1, max_batch} for ns in {0, max_blocks_per_seq})
+        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        # pinned host staging for step inputs: tokens, positions, slots, ctx, then the table
+        self.stage = torch.zeros(4 * B + B * max_blocks_per_seq, dtype=torch.int32, pin_memory=True)
+        self.graphs: dict = {}
+
+    # ---- the step -----------------------------------------------------------------------------
+    def _norm(self, h, w, b, x):
+        if self.spec.family == "gpt2":
+            K.layernorm(h, w, b, self.spec.eps, x=x)
+        else:
+            K.rmsnorm(h, w, self.spec.eps, x=x)
+
+    def _allreduce(self, t):
+        if self.world > 1:
+            torch.distributed.all_reduce(t, group=self.group)
+
+    @staticmethod
+    def linear_bytes(q: torch.Tensor, m: int, out_bytes: int, n_out: int) -> int:
+        """Algorithmic bytes of one INT8 linear launch: codes + scales + x (bf16) + y."""
+        n, k = q.shape
+        return n * k + 4 * n + 2 * m * k + out_bytes * m * n_out
+
+    def forward(self, b: int, n_shared_blocks: int = 0, compute_logits: bool = True, probe=None,
+                kv_tokens: int = 0) -> None:
+        """One decode step for the first ``b`` rows of the input buffers (tokens, positions,
+        slots, ctx, tables). Writes logits[:b] and next_tokens[:b] when compute_logits.
+
+        ``probe(kind, algorithmic_bytes)`` — optional context-manager factory wrapped around
+        each launch (per-kernel timing); ``kv_tokens`` is the unique KV token count the
+        attention launches read (for the probe's byte count)."""
+        s, w = self.spec, self.w
+        h, x = self.h[:b], self.x[:b]
+        tab, ctx = self.tables[:b], self.ctx[:b]
+        epi_res = K.EPI_ADD_F32 if self.rank == 0 else K.EPI_STORE_F32
+        P = probe if probe is not None else (lambda kind, nbytes: contextlib.nullcontext())
+        H, D = s.hidden, self.D
+        nqkv = (self.hq + 2 * self.hkv) * D
+        attn_bytes = kv_tokens * self.hkv * D * 2 * 2 + b * self.hq * D * (4 + 2)
+        with P("embed", b * H * 8):
+            K.embed(self.tokens[:b], self.positions[:b], w.embed, w.wpe, h)
+        for l, L in enumerate(w.layers):
+            with P("norm", b * H * 6):
+                self._norm(h, L.ln1_w, L.ln1_b, x)
+            with P("i8_linear", self.linear_bytes(L.qkv_q, b, 4, nqkv)):
+                K.i8_linear(x, L.qkv_q, L.qkv_s, L.qkv_b, y=self.qkv[:b], epilogue=K.EPI_STORE_F32)
+            with P("rope_kv_append", b * nqkv * 4 + b * self.hq * D * 4 + b * 2 * self.hkv * D * 2):
+                K.rope_kv_append(self.qkv[:b], self.positions[:b], self.cos_sin, self.slots[:b], self.hq,
+                                 self.hkv, self.D, self.pool.k[l], self.pool.v[l], q_out=self.q[:b])
+            with P("paged_attn", attn_bytes):
+                K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
+                                    n_shared_blocks=n_shared_blocks, out=self.attn[:b], workspace=self.workspace)
+            with P("i8_linear", self.linear_bytes(L.o_q, b, 8, H)):
+                K.i8_linear(self.attn[:b], L.o_q, L.o_s, L.o_b, y=h, epilogue=epi_res)
+            self._allreduce(h)
+            with P("norm", b * H * 6):
+                self._norm(h, L.ln2_w, L.ln2_b, x)
+            epi_mlp = K.EPI_GELU_BF16 if s.family == "gpt2" else K.EPI_SWIGLU_BF16
+            with P("i8_linear", self.linear_bytes(L.gu_q, b, 2, self.act.shape[1])):
+                K.i8_linear(x, L.gu_q, L.gu_s, L.gu_b, y=self.act[:b], epilogue=epi_mlp)
+            with P("i8_linear", self.linear_bytes(L.d_q, b, 8, H)):
+                K.i8_linear(self.act[:b], L.d_q, L.d_s, L.d_b, y=h, epilogue=epi_res)
+            self._allreduce(h)
+        if compute_logits:
+            with P("norm", b * H * 6):
+                self._norm(h, w.norm_w, w.norm_b, x)
+            with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, s.vocab)):
+                K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32)
+            with P("argmax", b * s.vocab * 4):
+                K.argmax_rows(self.logits[:b], out=self.next_tokens[:b])
+
+    def set_inputs(self, tokens, positions, slots, ctx, tables) -> int:
+        """Stage one step's inputs in pinned host memory and copy them to the static device
+        buffers (async on the current stream). Returns the batch size; also records the
+        host-to-device bytes of the step in ``self.h2d_bytes``."""
+        b = len(tokens)
+        if b > self.max_batch:
+            raise ValueError(f"batch {b} > max_batch {self.max_batch}")
+        t = torch.as_tensor(tables, dtype=torch.int32)
+        w = t.shape[1]
+        if w > self.max_blocks:
+            raise ValueError(f"block table of {w} blocks > {self.max_blocks}")
+        torch.cuda.current_stream(self.device).synchronize()  # the staging buffer may still be in flight
+        st = self.stage
+        B = self.max_batch
+        for i, v in enumerate((tokens, positions, slots, ctx)):
+            st[i * B:i * B + b] = torch.as_tensor(v, dtype=torch.int32)
+        tab = st[4 * B:4 * B + b * w].view(b, w)
+        tab.copy_(t)
+        for i, dst in enumerate((self.tokens, self.positions, self.slots, self.ctx)):
+            dst[:b].copy_(st[i * B:i * B + b], non_blocking=True)
+        self.tables[:b, :w].copy_(tab, non_blocking=True)
+        self.h2d_bytes = 4 * (4 * b + b * w)
+        return b
+
+    # ---- CUDA graphs -------------------------------------------------------------------------------
+    def capture(self, b: int, n_shared_blocks: int = 0, advance: bool = False,
+                compute_logits: bool = True) -> torch.cuda.CUDAGraph:
+        """Capture one decode step for batch ``b`` (plus, with ``advance``, the device-side
+        move to the next position: tokens = argmax, positions/ctx += 1, new slots)."""
+        key = (b, n_shared_blocks, advance, compute_logits)
+        if key in self.graphs:
+            return self.graphs[key]
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.forward(b, n_shared_blocks, compute_logits)  # warm-up: loads kernels, sets attributes
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.forward(b, n_shared_blocks, compute_logits)
+            if advance:
+                K.decode_advance(self.tokens[:b], self.next_tokens[:b], self.positions[:b], self.ctx[:b],
+                                 self.slots[:b], self.tables[:b])
+        self.graphs[key] = g
+        return g
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()

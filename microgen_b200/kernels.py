@@ -123,6 +123,8 @@ def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared
     _lib.call("mg_paged_decode_attn", _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables),
               max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks, float(scale), _ptr(out),
               _ptr(workspace if ws else None), ws, _stream())
+    if ws:
+        _lib.LAUNCHES[0] += 1  # the split-combine kernel
     return out
 
 

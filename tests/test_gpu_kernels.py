@@ -228,8 +228,6 @@ def _run_attn(q, kp, vp, tables, ctx, n_shared):
 def test_attention_vs_reference_fixture(tag):
     d = np.load(os.path.join(G, "attn_cases.npz"))
     q = d[f"{tag}_q"]
-    if q.shape[-1] not in (64, 128):
-        pytest.skip("kernel head_dim is 64 or 128")
     kp, vp = bf16_np(d[f"{tag}_kpool"]), bf16_np(d[f"{tag}_vpool"])
     got = _run_attn(q, kp, vp, d[f"{tag}_tables"], d[f"{tag}_ctx"], 0)
     close(got, d[f"{tag}_out"])
