@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (debug)")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
+    ap.add_argument("--profile", action="store_true",
+                    help="ncu mode: KV filled with random values instead of a prefill, no window centering, "
+                         "no probe / e2e / CPU legs")
     return ap.parse_args()
 
 
@@ -130,10 +134,9 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from microgen_b200.model_spec import ModelSpec, GPT2_SMALL, LLAMA_3B, QWEN_05B  # noqa: F401
+    from microgen_b200 import model_spec as MS
     wl = WORKLOADS[args.workload]
-    spec = ModelSpec(**globals()[wl["shape"]] if wl["shape"] in globals() else
-                     {"LLAMA_3B": LLAMA_3B, "QWEN_05B": QWEN_05B, "GPT2_SMALL": GPT2_SMALL}[wl["shape"]])
+    spec = MS.ModelSpec(**getattr(MS, wl["shape"]))
     ctx = wl["prompt"] + wl["decode"] // 2
     budget = min(90.0, max(10.0, 2.0 * (args.steps + args.warmup)))
     cb = cpu_baseline(spec, wl, ctx, budget_s=budget)
@@ -145,6 +148,26 @@ def run_reference(args) -> None:
         "config": {"workload": f"{args.workload}: {wl}", "tp": 1, "device": "host cpu"},
         "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def random_fill(be, prompts, n_shared):
+    """Profile mode: block tables as a prefill would leave them (shared prefix by reference
+    count), the KV pool filled with seeded random bf16 values instead of computed K/V."""
+    import torch
+    from microgen_b200.backends.b200 import PagedKVCache
+    b, p = prompts.shape
+    cache = PagedKVCache(be.allocator)
+    if n_shared:
+        cache.prefix = be.allocator.allocate_sequence("prefix", n_shared * 16)
+        cache.tables = [be.allocator.share_prefix(cache.prefix, n_shared, f"seq{i}", p) for i in range(b)]
+    else:
+        cache.tables = [be.allocator.allocate_sequence(f"seq{i}", p) for i in range(b)]
+    cache.n_shared_blocks = n_shared
+    g = torch.Generator(device=be.engine.pool.k.device).manual_seed(2)
+    for t in (be.engine.pool.k, be.engine.pool.v):
+        for l in range(t.shape[0]):
+            t[l].normal_(generator=g)
+    return cache
 
 
 def main():
@@ -174,10 +197,13 @@ def main():
     wl = dict(WORKLOADS[args.workload])
     if args.prompt:
         wl["prompt"], wl["shared"] = args.prompt, min(wl["shared"], args.prompt // 2)
-    spec = MS.ModelSpec(**getattr(MS, wl["shape"]))
+    shape = dict(getattr(MS, wl["shape"]))
+    if args.layers:
+        shape["layers"] = args.layers
+    spec = MS.ModelSpec(**shape)
     B, P, S, Dec = wl["batch"], wl["prompt"], wl["shared"], wl["decode"]
     W, Kst = args.warmup, args.steps
-    skip = max(0, Dec // 2 - W - Kst // 2)
+    skip = 0 if args.profile else max(0, Dec // 2 - W - Kst // 2)
     run = skip + W + Kst
     max_seq = P + max(Dec, run) + 16
     max_blocks = (max_seq + 15) // 16
@@ -198,10 +224,14 @@ def main():
     prompts = torch.stack([torch.cat([shared, torch.randint(0, spec.vocab, (P - S,), generator=g)])
                            for _ in range(B)])
     t0 = time.time()
-    logits, cache = be.prefill(prompts)
+    if args.profile:
+        cache = random_fill(be, prompts, n_shared)
+        first = prompts[:, -1].to(torch.int32)
+    else:
+        logits, cache = be.prefill(prompts)
+        first = be.sample(logits)[:, 0].to(torch.int32).cpu()
     torch.cuda.synchronize()
     t_prefill = time.time() - t0
-    first = be.sample(logits)[:, 0].to(torch.int32).cpu()
 
     # ---- device-timed decode: graph replays, inputs resident, device-side advance --------------
     alloc = be.allocator
@@ -248,7 +278,16 @@ def main():
     mean_pos = P + skip + W + (Kst - 1) / 2.0
     kv_tokens = n_shared * 16 + B * (int(mean_pos) + 1 - n_shared * 16)
 
-    # ---- per-kernel device time (probe pass, eager, CUDA events on the launch stream) ----------
+    if args.profile:
+        eng.release_graphs()
+        if rank == 0:
+            print(json.dumps({"profile": args.workload, "ms_per_step": round(ms, 4), "value": round(value, 1)}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # ---- per-kernel device time (probe pass: CUDA events on the launch stream around each launch;
+    # a short spin kernel ahead of each launch keeps the host's launch latency out of the interval)
     stats: dict = {}
 
     class Probe:
@@ -256,6 +295,7 @@ def main():
             self.kind, self.nbytes = kind, nbytes
 
         def __enter__(self):
+            torch.cuda._sleep(40000)
             self.a = torch.cuda.Event(enable_timing=True)
             self.b = torch.cuda.Event(enable_timing=True)
             self.a.record(torch.cuda.current_stream())

@@ -71,6 +71,16 @@ int mg_i8_linear_simt(const void* x, int64_t m, int64_t k, int64_t ldx, const in
 int mg_i8_linear_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
                     const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, int split_k, void* stream);
 
+/* Tile-packed codes: the weight stored as contiguous 16 KB blocks, one per 128-row x 128-column
+ * tile, tiles in (row-tile, k-block) order, zero-padded to multiples of 128:
+ *   packed[((t*KB + kb)*128 + r)*128 + c] = q[(t*128 + r)*k + kb*128 + c],  KB = ceil(k/128).
+ * Every weight load of the linear is then one sequential 16 KB burst. Pack once at load time. */
+int64_t mg_i8_packed_bytes(int64_t n, int64_t k);
+int mg_i8_pack_weights(const int8_t* q, int64_t n, int64_t k, int8_t* packed, void* stream);
+/* mg_i8_linear_tc on tile-packed codes (same contract otherwise; split_k 0 = automatic). */
+int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed, const float* scales,
+                        const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, int split_k, void* stream);
+
 /* ---- paged KV: RoPE + append (kv_cache.py:76-127, as one slot write per token) ------------ */
 /* qkv fp32 [b, (hq+2*hkv)*d] (row stride ld_qkv): q heads, then k heads, then v heads.
  * rope: cos_sin fp32 [max_pos, d] (cos of the d/2 frequencies, then sin), NULL = no rotation.

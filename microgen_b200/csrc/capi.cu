@@ -1,10 +1,20 @@
 // C-ABI plumbing: status strings, error words, version.
+#include <cstdlib>
+
 #include "common.cuh"
 
 __device__ int g_mg_dev_error = 0;
 __device__ int g_mg_dev_error_info = 0;
 
 static thread_local int t_last_cuda_error = 0;
+
+bool mg_pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("MG_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int mg_set_cuda_error(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);

@@ -35,6 +35,45 @@ int mg_set_cuda_error(cudaError_t e);
 static inline cudaStream_t mg_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of the decode step is launched with programmatic
+// stream serialization: it may start while its predecessor drains, signals its own dependents at
+// entry (griddep_launch), and calls griddep_wait before it touches anything a predecessor
+// writes. Every kernel waits (even on early-exit paths), so the completion of a kernel implies
+// the completion of the whole chain before it. MG_PDL=0 in the environment turns it off.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool mg_pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t mg_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                    unsigned cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  unsigned n = 0;
+  if (cluster > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = cluster;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (mg_pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Small math helpers
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
@@ -71,11 +110,19 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, fl
 
 // Four signed int8 -> two bf16x2 words (exact: |b| <= 128 fits bf16's 8-bit significand).
 // The fp32 values are small integers, so truncating to the upper 16 bits is exact.
+// 8 instructions per 4 bytes: byte b is placed in a bf16 with bits 0x43 : (b & 0x7F), i.e. the value
+// 128 + (b & 0x7F); subtracting 128 (b >= 0) or 256 (b < 0) — a second bf16 whose bit 7 is b's sign
+// bit — leaves b. Every operand and the difference are small integers, so the bf16 subtraction is exact.
+__device__ __forceinline__ uint32_t i8x2_to_bf16x2(uint32_t p) {  // p: halves hold bytes (0x00bb)
+  const uint32_t v = (p & 0x007F007Fu) | 0x43004300u;
+  const uint32_t m = (p & 0x00800080u) | 0x43004300u;
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(m));
+  return r;
+}
 __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  float f0, f1, f2, f3;
-  i8x4_to_f32(w, f0, f1, f2, f3);
-  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+  lo = i8x2_to_bf16x2(__byte_perm(w, 0u, 0x4140));  // b0 (low half), b1
+  hi = i8x2_to_bf16x2(__byte_perm(w, 0u, 0x4342));  // b2, b3
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -106,6 +153,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking probe of a phase (no suspension), for threads that poll several barriers.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -224,16 +283,17 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
+// Distributed-shared-memory loads. `volatile` keeps them on their side of the cluster barriers
+// (themselves volatile asm); no memory clobber, so independent loads can be issued back to back.
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+               : "r"(addr));
   return v;
 }
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }

@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32) i8_gemv_simt(const __nv_bfloa
                                                                  const float* __restrict__ scales,
                                                                  const float* __restrict__ bias, int64_t N, void* y,
                                                                  int64_t ldy, int epi) {
+  griddep_launch();
+  griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool swiglu = epi == MG_EPI_SWIGLU_BF16;
   const int64_t nout = swiglu ? N / 2 : N;
@@ -146,21 +148,29 @@ __global__ void __launch_bounds__(kSimtWarps * 32) i8_gemv_simt(const __nv_bfloa
 // ------------------------------------------------------------------------------------------------
 constexpr int kBN = 128;          // weight rows per tile (MMA M)
 constexpr int kBK = 128;          // K per pipeline stage
-constexpr int kTcThreads = 192;   // warps 0-3 convert + epilogue, warp 4 TMA, warp 5 MMA
+constexpr int kConvWarps = 8;     // warp w converts rows 32*(w%4).. (its TMEM lane quarter), K half w/4
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kTcThreads = 320;
 constexpr uint32_t kWStageBytes = kBN * kBK;  // int8 tile
 
 template <int MP>
 struct TcCfg {
-  static constexpr int kStages = MP <= 32 ? 4 : (MP <= 64 ? 3 : 2);
-  static constexpr uint32_t kXStageBytes = MP * kBK * 2;  // bf16
-  static constexpr uint32_t kStageBytes = kWStageBytes + kXStageBytes;
-  static constexpr uint32_t kPipeBytes = kStages * kStageBytes;
+  // Weight ring (16 KB int8 stages, freed as soon as the converters hold the bytes in registers)
+  // and activation ring (MP x 128 bf16 stages, freed by the MMA commit), sized to ~96 KB per CTA so
+  // two CTAs share an SM for MP <= 128 (one CTA with ~192 KB for MP = 256).
+  static constexpr int kWStages = MP <= 32 ? 5 : (MP <= 64 ? 4 : (MP <= 128 ? 2 : 4));
+  static constexpr int kXStages = MP <= 16 ? 3 : 2;
+  static constexpr int kABufs = MP <= 64 ? 3 : 2;                   // bf16 A tiles in TMEM (64 columns each)
+  static constexpr uint32_t kXStageBytes = MP * kBK * 2;            // bf16
+  static constexpr uint32_t kXOffset = kWStages * kWStageBytes;
+  static constexpr uint32_t kPipeBytes = kXOffset + kXStages * kXStageBytes;
   static constexpr uint32_t kRedBytes = MP * kBN * 4;
   static constexpr uint32_t kMainBytes = kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes;
   static constexpr uint32_t kBarOffset = kMainBytes;
   static constexpr uint32_t kSmemBytes = kMainBytes + 256 + 1024;  // barriers + alignment slack
-  static constexpr uint32_t kAccCol = 128;                          // A buffers use columns [0,128)
-  static constexpr uint32_t kTmemCols = (128 + MP) <= 256 ? 256 : 512;
+  static constexpr uint32_t kAccCol = kABufs * 64;
+  static constexpr uint32_t kTmemCols = (kAccCol + MP) <= 256 ? 256 : 512;
   // D=fp32 (bit 4), A=B=bf16 (bits 7, 10), K-major A and B, N = MP, M = 128.
   static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MP >> 3) << 17) |
                                      ((uint32_t)(kBN >> 4) << 24);
@@ -180,18 +190,23 @@ template <int MP>
 __global__ void __launch_bounds__(kTcThreads, 1)
     i8_gemm_tc(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, int M, int K,
                int64_t N, const float* __restrict__ scales, const float* __restrict__ bias, void* y, int64_t ldy,
-               int epi, int split) {
+               int epi, int split, int packed) {
   using C = TcCfg<MP>;
-  constexpr int S = C::kStages;
+  constexpr int SW = C::kWStages;
+  constexpr int SX = C::kXStages;
+  constexpr int NA = C::kABufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
-  uint64_t* empty = full + S;
-  uint64_t* afull = empty + S;
-  uint64_t* aempty = afull + 2;
-  uint64_t* accfull = aempty + 2;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* wempty = wfull + SW;
+  uint64_t* xfull = wempty + SW;
+  uint64_t* xempty = xfull + SX;
+  uint64_t* afull = xempty + SX;
+  uint64_t* aempty = afull + NA;
+  uint64_t* accfull = aempty + NA;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accfull + 1);
 
+  griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = split > 1 ? cluster_ctarank() : 0;
   const int tile = blockIdx.x / split;
@@ -200,24 +215,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int kb_begin = (int)((int64_t)crank * kb_total / split);
   const int kb_end = (int)((int64_t)(crank + 1) * kb_total / split);
   const int nk = kb_end - kb_begin;
+  // Weight tile (tile, kb): row-major codes -> box at (kb*128, tile*128); tile-packed codes (every
+  // 128x128 tile stored as one contiguous 16 KB block) -> box at (0, (tile*kb_total + kb)*128).
+  auto w_c0 = [&](int kb) { return packed ? 0 : kb * kBK; };
+  auto w_c1 = [&](int kb) { return packed ? (tile * kb_total + kb) * kBN : tile * kBN; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 5);
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], kConvWarps);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&afull[b], 4);
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int b = 0; b < NA; ++b) {
+      mbar_init(&afull[b], kConvWarps);
       mbar_init(&aempty[b], 1);
     }
     mbar_init(accfull, 1);
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_holder, C::kTmemCols);
     tmem_relinquish();
   }
@@ -227,135 +250,181 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = *tmem_holder;
   bool ok = true;
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
+  if (warp == kProducerWarp) {
+    // ---------------- TMA producer: one thread feeding both rings ----------------
     if (lane == 0) {
-      for (int i = 0; i < nk && ok; ++i) {
-        const int s = i % S;
-        if (i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1, 1);
-        if (!ok) break;
-        uint8_t* sw = smem + s * C::kStageBytes;
-        uint8_t* sx = sw + kWStageBytes;
-        const int k0 = (kb_begin + i) * kBK;
-        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        tma_load_2d(sw, &tmap_w, &full[s], k0, tile * kBN);
-        tma_load_2d(sx, &tmap_x, &full[s], k0, mtile * MP);
-        tma_load_2d(sx + MP * 128, &tmap_x, &full[s], k0 + 64, mtile * MP);
+      // Weight tiles do not depend on the previous kernel: the first weight stages are in flight
+      // before the wait on the predecessor; activation tiles are only loaded after it.
+      int iw = 0, ix = 0;
+      for (; iw < nk && iw < SW; ++iw) {
+        mbar_arrive_expect_tx(&wfull[iw], kWStageBytes);
+        tma_load_2d(smem + iw * kWStageBytes, &tmap_w, &wfull[iw], w_c0(kb_begin + iw), w_c1(kb_begin + iw));
+      }
+      griddep_wait();
+      uint32_t polls = 0;
+      while ((iw < nk || ix < nk) && ok) {
+        bool progressed = false;
+        if (ix < nk && (ix < SX || mbar_test_wait(&xempty[ix % SX], ((ix / SX) - 1) & 1))) {
+          const int s = ix % SX;
+          uint8_t* sx = smem + C::kXOffset + s * C::kXStageBytes;
+          const int k0 = (kb_begin + ix) * kBK;
+          mbar_arrive_expect_tx(&xfull[s], C::kXStageBytes);
+          tma_load_2d(sx, &tmap_x, &xfull[s], k0, mtile * MP);
+          tma_load_2d(sx + MP * 128, &tmap_x, &xfull[s], k0 + 64, mtile * MP);
+          ++ix;
+          progressed = true;
+        }
+        if (iw < nk && mbar_test_wait(&wempty[iw % SW], ((iw / SW) - 1) & 1)) {
+          const int s = iw % SW;
+          mbar_arrive_expect_tx(&wfull[s], kWStageBytes);
+          tma_load_2d(smem + s * kWStageBytes, &tmap_w, &wfull[s], w_c0(kb_begin + iw), w_c1(kb_begin + iw));
+          ++iw;
+          progressed = true;
+        }
+        if (!progressed) {
+          if (++polls > MG_SPIN_LIMIT) {
+            mg_record_error(MG_ERR_TIMEOUT, 1);
+            ok = false;
+          }
+          __nanosleep(32);
+        }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       for (int i = 0; i < nk && ok; ++i) {
-        const int s = i % S, ab = i & 1;
-        ok = mbar_wait(&full[s], (i / S) & 1, 2) && mbar_wait(&afull[ab], (i >> 1) & 1, 3);
+        const int s = i % SX, ab = i % NA;
+        ok = mbar_wait(&xfull[s], (i / SX) & 1, 2) && mbar_wait(&afull[ab], (i / NA) & 1, 3);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t sx = smem_u32(smem + s * C::kStageBytes + kWStageBytes);
+        const uint32_t sx = smem_u32(smem + C::kXOffset + s * C::kXStageBytes);
 #pragma unroll
         for (int j = 0; j < kBK / 16; ++j) {
           const uint32_t a_t = tmem + (uint32_t)(ab * 64 + j * 8);
           const uint64_t bd = desc_sw128(sx + (uint32_t)((j >> 2) * MP * 128 + (j & 3) * 32));
           tc_mma_ts(tmem + C::kAccCol, a_t, bd, C::kIdesc, (i > 0 || j > 0) ? 1u : 0u);
         }
-        tc_commit(&empty[s]);
+        tc_commit(&xempty[s]);
         tc_commit(&aempty[ab]);
       }
       tc_commit(accfull);
     }
   } else {
-    // ---------------- converters: int8 smem row -> bf16 TMEM lane ----------------
-    const int t = threadIdx.x;  // weight row within the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // ---------------- converters: half an int8 smem row -> 32 bf16x2 TMEM columns ----------------
+    const int row = (warp & 3) * 32 + lane;   // weight row within the tile == TMEM lane
+    const int hh = warp >> 2;                 // K half: bytes [64*hh, 64*hh + 64)
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     for (int i = 0; i < nk && ok; ++i) {
-      const int s = i % S, ab = i & 1;
-      ok = mbar_wait(&full[s], (i / S) & 1, 4);
-      if (ok && i >= 2) ok = mbar_wait(&aempty[ab], ((i >> 1) - 1) & 1, 5);
+      const int s = i % SW, ab = i % NA;
+      ok = mbar_wait(&wfull[s], (i / SW) & 1, 4);
       if (!ok) break;
-      const uint8_t* row = smem + s * C::kStageBytes + t * 128;
+      const uint8_t* src = smem + s * kWStageBytes + row * 128;
+      uint4 v[4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t r[32];
+      for (int c4 = 0; c4 < 4; ++c4) v[c4] = *reinterpret_cast<const uint4*>(src + (((hh * 4 + c4) ^ (row & 7)) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[s]);  // the bytes are in registers: the stage can refill
+      if (i >= NA) ok = mbar_wait(&aempty[ab], ((i / NA) - 1) & 1, 5);
+      if (!ok) break;
+      uint32_t r[32];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const int c = h * 4 + c4;
-          const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (t & 7)) << 4));
-          i8x4_to_bf16x4(v.x, r[c4 * 8 + 0], r[c4 * 8 + 1]);
-          i8x4_to_bf16x4(v.y, r[c4 * 8 + 2], r[c4 * 8 + 3]);
-          i8x4_to_bf16x4(v.z, r[c4 * 8 + 4], r[c4 * 8 + 5]);
-          i8x4_to_bf16x4(v.w, r[c4 * 8 + 6], r[c4 * 8 + 7]);
-        }
-        tmem_st32(tmem + lane_base + (uint32_t)(ab * 64 + h * 32), r);
+      for (int c4 = 0; c4 < 4; ++c4) {
+        i8x4_to_bf16x4(v[c4].x, r[c4 * 8 + 0], r[c4 * 8 + 1]);
+        i8x4_to_bf16x4(v[c4].y, r[c4 * 8 + 2], r[c4 * 8 + 3]);
+        i8x4_to_bf16x4(v[c4].z, r[c4 * 8 + 4], r[c4 * 8 + 5]);
+        i8x4_to_bf16x4(v[c4].w, r[c4 * 8 + 6], r[c4 * 8 + 7]);
       }
+      tmem_st32(tmem + lane_base + (uint32_t)(ab * 64 + hh * 32), r);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&empty[s]);
-        mbar_arrive(&afull[ab]);
-      }
+      if (lane == 0) mbar_arrive(&afull[ab]);
     }
   }
 
   // ---------------- epilogue: TMEM -> shared (fp32, [MP][128]) ----------------
+  griddep_wait();  // (returns at once: the producer already waited) every thread orders its y access
   float* red = reinterpret_cast<float*>(smem);
-  if (warp < 4) {
-    const int t = threadIdx.x;
+  constexpr int kColsPerWarp = MP >= 64 ? MP / 2 : MP;  // warps 4-7 take the upper half when MP >= 64
+  if (warp < kConvWarps && (MP >= 64 || warp < 4)) {
+    const int row = (warp & 3) * 32 + lane;
+    const int c_begin = MP >= 64 ? (warp >> 2) * kColsPerWarp : 0;
     if (nk > 0 && mbar_wait(accfull, 0, 6)) {
       tc_fence_after();
-      const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
 #pragma unroll 1
-      for (int c0 = 0; c0 < MP; c0 += 32) {
+      for (int c0 = c_begin; c0 < c_begin + kColsPerWarp; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + C::kAccCol + (uint32_t)c0, r);
         tc_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) red[(c0 + j) * kBN + t] = __uint_as_float(r[j]);
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < c_begin + kColsPerWarp) red[(c0 + j) * kBN + row] = __uint_as_float(r[j]);
       }
     } else {
-      for (int c = 0; c < MP; ++c) red[c * kBN + t] = 0.f;
+      for (int c = c_begin; c < c_begin + kColsPerWarp; ++c) red[c * kBN + row] = 0.f;
     }
     tc_fence_before();
   }
   if (split > 1) cluster_sync_all(); else __syncthreads();
 
   // ---------------- split-K reduction + epilogue ----------------
-  if (warp < 4) {
+  // CTA `crank` owns token columns ml ≡ crank (mod split); within the CTA, converter thread t takes
+  // weight row t % 128 and every second owned column (t / 128). For SwiGLU only rows < 64 are
+  // active, each reducing its gate/up pair (t, t+64). All `split` partials of an element are loaded
+  // before any is added (one distributed-shared-memory latency per element), and the sum runs in
+  // fixed CTA order (deterministic).
+  if (warp < kConvWarps) {
     const int t = threadIdx.x;
+    const int half = t >> 7;
     const int m_base = mtile * MP;
     const int m_valid = min(MP, M - m_base);
     const bool swiglu = epi == MG_EPI_SWIGLU_BF16;
     const uint32_t red_addr = smem_u32(red);
-    for (int ml = (int)crank; ml < m_valid; ml += split) {
-      const int m = m_base + ml;
-      if (!swiglu) {
-        const int64_t n = (int64_t)tile * kBN + t;
-        float v = 0.f;
-        for (int j = 0; j < split; ++j) {
-          const uint32_t a = red_addr + (uint32_t)((ml * kBN + t) * 4);
-          v += split > 1 ? ld_dsmem_f32(mapa_shared(a, j)) : red[ml * kBN + t];
+    const int r0 = swiglu ? (t & 63) : (t & 127);
+    const int64_t n0 = (int64_t)tile * kBN + r0;
+    const int64_t n1 = n0 + 64;  // SwiGLU up row
+    const bool active = swiglu ? ((t & 127) < 64 && n1 < N) : (n0 < N);
+    const float s0 = active ? scales[n0] : 0.f;
+    const float b0 = (active && bias) ? bias[n0] : 0.f;
+    const float s1 = (active && swiglu) ? scales[n1] : 0.f;
+    const float b1 = (active && swiglu && bias) ? bias[n1] : 0.f;
+    uint32_t rbase[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rbase[j] = (split > 1 && j < split) ? mapa_shared(red_addr, j) : red_addr;
+    if (active) {
+      for (int ml = (int)crank + half * split; ml < m_valid; ml += 2 * split) {
+        const int m = m_base + ml;
+        const uint32_t off0 = (uint32_t)((ml * kBN + r0) * 4);
+        float p0[8], p1[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          p0[j] = 0.f;
+          p1[j] = 0.f;
+          if (j < split) {
+            p0[j] = ld_dsmem_f32(rbase[j] + off0);
+            if (swiglu) p1[j] = ld_dsmem_f32(rbase[j] + off0 + 64 * 4);
+          }
         }
-        if (n < N) store_out(epi, y, (int64_t)m * ldy + n, v * scales[n] + (bias ? bias[n] : 0.f));
-      } else if (t < 64) {
-        const int64_t rg = (int64_t)tile * kBN + t, ru = rg + 64;
-        float g = 0.f, u = 0.f;
-        for (int j = 0; j < split; ++j) {
-          const uint32_t ag = red_addr + (uint32_t)((ml * kBN + t) * 4);
-          const uint32_t au = ag + 64 * 4;
-          g += split > 1 ? ld_dsmem_f32(mapa_shared(ag, j)) : red[ml * kBN + t];
-          u += split > 1 ? ld_dsmem_f32(mapa_shared(au, j)) : red[ml * kBN + t + 64];
+        float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v0 += p0[j];
+          v1 += p1[j];
         }
-        if (ru < N) {
-          const float gv = g * scales[rg] + (bias ? bias[rg] : 0.f);
-          const float uv = u * scales[ru] + (bias ? bias[ru] : 0.f);
-          static_cast<__nv_bfloat16*>(y)[(int64_t)m * ldy + (int64_t)tile * 64 + t] =
+        if (!swiglu) {
+          store_out(epi, y, (int64_t)m * ldy + n0, v0 * s0 + b0);
+        } else {
+          const float gv = v0 * s0 + b0, uv = v1 * s1 + b1;
+          static_cast<__nv_bfloat16*>(y)[(int64_t)m * ldy + (int64_t)tile * 64 + r0] =
               __float2bfloat16_rn(silu_f(gv) * uv);
         }
       }
     }
   }
   if (split > 1) cluster_sync_all(); else __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
@@ -416,7 +485,8 @@ int auto_split(int64_t tiles, int kblocks, int ctas_per_sm) {
 
 template <int MP>
 int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
-              const float* bias, int64_t n, void* y, int64_t ldy, int epi, int split, cudaStream_t st) {
+              const float* bias, int64_t n, void* y, int64_t ldy, int epi, int split, cudaStream_t st,
+              bool packed) {
   using C = TcCfg<MP>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -424,7 +494,9 @@ int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
     attr_done = true;
   }
   CUtensorMap mw, mx;
-  int rc = make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t)k, (uint64_t)n, (uint64_t)k, kBK, kBN);
+  const uint64_t packed_rows = (uint64_t)((n + kBN - 1) / kBN) * ((k + kBK - 1) / kBK) * kBN;
+  int rc = packed ? make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, kBK, packed_rows, kBK, kBK, kBN)
+                  : make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t)k, (uint64_t)n, (uint64_t)k, kBK, kBN);
   if (rc) return rc;
   rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)k, (uint64_t)m, (uint64_t)ldx * 2, 64, MP);
   if (rc) return rc;
@@ -435,20 +507,40 @@ int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
   if (split > kblocks) split = kblocks;
   if (split < 1) split = 1;
   if (split > 8 || tiles * split > 0x7fffffff || mtiles > 65535) return MG_ERR_UNSUPPORTED;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(tiles * split), (unsigned)mtiles, 1);
-  cfg.blockDim = dim3(kTcThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = split;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, i8_gemm_tc<MP>, mw, mx, (int)m, (int)k, n, scales, bias, y, ldy, epi, split));
+  MG_CUDA_TRY(mg_launch(i8_gemm_tc<MP>, dim3((unsigned)(tiles * split), (unsigned)mtiles, 1), dim3(kTcThreads),
+                        C::kSmemBytes, st, (unsigned)split, mw, mx, (int)m, (int)k, n, scales, bias, y, ldy, epi,
+                        split, packed ? 1 : 0));
   return MG_OK;
+}
+
+int dispatch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
+                const float* bias, int64_t n, void* y, int64_t ldy, int epi, int split_k, cudaStream_t st,
+                bool packed) {
+#define MG_TC(MPV) launch_tc<MPV>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st, packed)
+  if (m <= 16) return MG_TC(16);
+  if (m <= 32) return MG_TC(32);
+  if (m <= 64) return MG_TC(64);
+  if (m <= 128) return MG_TC(128);
+  return MG_TC(256);
+#undef MG_TC
+}
+
+// [tiles][kblocks][128 rows][128 B]: packed[((t*KB + kb)*128 + r)*128 + c] = q[(t*128 + r)*k + kb*128 + c],
+// zero where the row or column is past the matrix. One thread per 16 bytes.
+__global__ void pack_tiles_kernel(const int8_t* __restrict__ q, int64_t n, int64_t k, int8_t* __restrict__ out,
+                                  int64_t total16) {
+  griddep_wait();  // no early trigger: the linears that follow prefetch these codes before waiting
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total16) return;
+  const int64_t kb_total = (k + kBK - 1) / kBK;
+  const int64_t c16 = i & 7;          // 16-byte chunk within the 128-byte tile row
+  const int64_t r = (i >> 3) & 127;   // tile row
+  const int64_t blk = i >> 10;        // t * KB + kb
+  const int64_t t = blk / kb_total, kb = blk % kb_total;
+  const int64_t row = t * kBN + r, col = kb * kBK + c16 * 16;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (row < n && col < k) v = *reinterpret_cast<const uint4*>(q + row * k + col);  // k % 16 == 0
+  reinterpret_cast<uint4*>(out)[i] = v;
 }
 
 int check_linear_args(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
@@ -474,9 +566,8 @@ extern "C" int mg_i8_linear_simt(const void* x, int64_t m, int64_t k, int64_t ld
   const int64_t nout = epi == MG_EPI_SWIGLU_BF16 ? n / 2 : n;
   const int64_t blocks = (nout + kSimtWarps - 1) / kSimtWarps;
   if (blocks > 0x7fffffff) return MG_ERR_UNSUPPORTED;
-  i8_gemv_simt<<<(unsigned)blocks, kSimtWarps * 32, 0, mg_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, (int)m, (int)k, q, scales, bias, n, y, ldy, epi);
-  MG_LAUNCH_CHECK();
+  MG_CUDA_TRY(mg_launch(i8_gemv_simt, dim3((unsigned)blocks), dim3(kSimtWarps * 32), 0, mg_stream(stream), 1,
+                        static_cast<const __nv_bfloat16*>(x), ldx, (int)m, (int)k, q, scales, bias, n, y, ldy, epi));
   return MG_OK;
 }
 
@@ -487,12 +578,33 @@ extern "C" int mg_i8_linear_tc(const void* x, int64_t m, int64_t k, int64_t ldx,
   if (rc) return rc;
   if (m == 0) return MG_OK;
   if (split_k < 0 || split_k > 8) return MG_ERR_INVALID_ARG;
-  cudaStream_t st = mg_stream(stream);
-  if (m <= 16) return launch_tc<16>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st);
-  if (m <= 32) return launch_tc<32>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st);
-  if (m <= 64) return launch_tc<64>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st);
-  if (m <= 128) return launch_tc<128>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st);
-  return launch_tc<256>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st);
+  return dispatch_tc(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, mg_stream(stream), false);
+}
+
+extern "C" int64_t mg_i8_packed_bytes(int64_t n, int64_t k) {
+  if (n <= 0 || k <= 0) return 0;
+  return ((n + kBN - 1) / kBN) * kBN * ((k + kBK - 1) / kBK) * kBK;
+}
+
+extern "C" int mg_i8_pack_weights(const int8_t* q, int64_t n, int64_t k, int8_t* packed, void* stream) {
+  if (!q || !packed || n <= 0 || k <= 0 || k % 16) return MG_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(packed)) & 15) return MG_ERR_INVALID_ARG;
+  const int64_t total16 = mg_i8_packed_bytes(n, k) / 16;
+  const int64_t blocks = (total16 + 255) / 256;
+  if (blocks > 0x7fffffff) return MG_ERR_UNSUPPORTED;
+  MG_CUDA_TRY(mg_launch(pack_tiles_kernel, dim3((unsigned)blocks), dim3(256), 0, mg_stream(stream), 1, q, n, k,
+                        packed, total16));
+  return MG_OK;
+}
+
+extern "C" int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                                   const float* scales, const float* bias, int64_t n, void* y, int64_t ldy, int epi,
+                                   int split_k, void* stream) {
+  int rc = check_linear_args(x, m, k, ldx, packed, scales, n, y, ldy, epi);
+  if (rc) return rc;
+  if (m == 0) return MG_OK;
+  if (split_k < 0 || split_k > 8) return MG_ERR_INVALID_ARG;
+  return dispatch_tc(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, split_k, mg_stream(stream), true);
 }
 
 extern "C" int mg_i8_linear(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,

@@ -36,6 +36,9 @@ __device__ __forceinline__ float block_reduce_max(float v, float* red) {
 // max|w| is exact in any order, the divisions are IEEE (__fdiv_rn), rintf rounds half to even.
 __global__ void quantize_rows_kernel(const float* __restrict__ w, int64_t k, int8_t* __restrict__ q,
                                      float* __restrict__ scales) {
+  // no early trigger: a following linear may prefetch the weights this kernel writes
+ 
+  griddep_wait();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const float* wr = w + row * k;
@@ -52,38 +55,98 @@ __global__ void quantize_rows_kernel(const float* __restrict__ w, int64_t k, int
   }
 }
 
-__global__ void rmsnorm_kernel(const float* __restrict__ h, const float* __restrict__ w, int n, float eps,
-                               __nv_bfloat16* __restrict__ x) {
+// Row norms, single pass: every thread loads its float4s (row and weight) up front, the row
+// statistic is block-reduced, and the output is written from registers. n % 4 == 0, n <= 4*256*kMaxV.
+constexpr int kNormMaxV = 8;
+
+__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* p, float a, float b, float c, float d) {
+  uint2 v;
+  v.x = pack_bf16x2(a, b);
+  v.y = pack_bf16x2(c, d);
+  *reinterpret_cast<uint2*>(p) = v;
+}
+
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const float* __restrict__ h,
+                                                               const float* __restrict__ w, int n, float eps,
+                                                               __nv_bfloat16* __restrict__ x) {
+  griddep_launch();
+  griddep_wait();
   __shared__ float red[32];
-  const float* hr = h + (int64_t)blockIdx.x * n;
+  const int nv = n >> 2;
+  const float4* hr = reinterpret_cast<const float4*>(h + (int64_t)blockIdx.x * n);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4 hv[kNormMaxV], wv[kNormMaxV];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += hr[i] * hr[i];
+#pragma unroll
+  for (int i = 0; i < kNormMaxV; ++i) {
+    const int idx = threadIdx.x + i * kRowThreads;
+    if (idx < nv) {
+      hv[i] = hr[idx];
+      wv[i] = wr[idx];
+      ss += hv[i].x * hv[i].x + hv[i].y * hv[i].y + hv[i].z * hv[i].z + hv[i].w * hv[i].w;
+    }
+  }
   ss = block_reduce_sum(ss, red);
   const float inv = rsqrtf(ss / (float)n + eps);
   __nv_bfloat16* xr = x + (int64_t)blockIdx.x * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __float2bfloat16_rn(w[i] * (hr[i] * inv));
+#pragma unroll
+  for (int i = 0; i < kNormMaxV; ++i) {
+    const int idx = threadIdx.x + i * kRowThreads;
+    if (idx < nv)
+      store_bf16x4(xr + 4 * idx, wv[i].x * (hv[i].x * inv), wv[i].y * (hv[i].y * inv), wv[i].z * (hv[i].z * inv),
+                   wv[i].w * (hv[i].w * inv));
+  }
 }
 
-__global__ void layernorm_kernel(const float* __restrict__ h, const float* __restrict__ w,
-                                 const float* __restrict__ b, int n, float eps, __nv_bfloat16* __restrict__ x) {
+__global__ void __launch_bounds__(kRowThreads) layernorm_kernel(const float* __restrict__ h,
+                                                                 const float* __restrict__ w,
+                                                                 const float* __restrict__ b, int n, float eps,
+                                                                 __nv_bfloat16* __restrict__ x) {
+  griddep_launch();
+  griddep_wait();
   __shared__ float red[32];
-  const float* hr = h + (int64_t)blockIdx.x * n;
+  const int nv = n >> 2;
+  const float4* hr = reinterpret_cast<const float4*>(h + (int64_t)blockIdx.x * n);
+  float4 hv[kNormMaxV];
   float s = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) s += hr[i];
+#pragma unroll
+  for (int i = 0; i < kNormMaxV; ++i) {
+    const int idx = threadIdx.x + i * kRowThreads;
+    if (idx < nv) {
+      hv[i] = hr[idx];
+      s += hv[i].x + hv[i].y + hv[i].z + hv[i].w;
+    }
+  }
   const float mean = block_reduce_sum(s, red) / (float)n;
   float v = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float d = hr[i] - mean;
-    v += d * d;
+#pragma unroll
+  for (int i = 0; i < kNormMaxV; ++i) {
+    const int idx = threadIdx.x + i * kRowThreads;
+    if (idx < nv) {
+      const float a = hv[i].x - mean, c = hv[i].y - mean, d = hv[i].z - mean, e = hv[i].w - mean;
+      v += a * a + c * c + d * d + e * e;
+    }
   }
   const float inv = rsqrtf(block_reduce_sum(v, red) / (float)n + eps);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  const float4* br = reinterpret_cast<const float4*>(b);
   __nv_bfloat16* xr = x + (int64_t)blockIdx.x * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __float2bfloat16_rn((hr[i] - mean) * inv * w[i] + b[i]);
+#pragma unroll
+  for (int i = 0; i < kNormMaxV; ++i) {
+    const int idx = threadIdx.x + i * kRowThreads;
+    if (idx < nv) {
+      const float4 wv = wr[idx], bv = br[idx];
+      store_bf16x4(xr + 4 * idx, (hv[i].x - mean) * inv * wv.x + bv.x, (hv[i].y - mean) * inv * wv.y + bv.y,
+                   (hv[i].z - mean) * inv * wv.z + bv.z, (hv[i].w - mean) * inv * wv.w + bv.w);
+    }
+  }
 }
 
 __global__ void embed_kernel(const int32_t* __restrict__ tokens, const int32_t* __restrict__ positions,
                              const float* __restrict__ wte, const float* __restrict__ wpe, int hidden, int64_t vocab,
                              int max_pos, float* __restrict__ h) {
+  griddep_launch();
+  griddep_wait();
   const int i = blockIdx.x;
   const int tok = tokens[i];
   if (tok < 0 || tok >= vocab) {
@@ -103,59 +166,57 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const int32_t* 
   for (int j = threadIdx.x; j < hidden; j += blockDim.x) hr[j] = e[j] + (wpe ? wpe[(int64_t)pos * hidden + j] : 0.f);
 }
 
-// One CTA per token. Heads [0,hq) are queries, [hq,hq+hkv) keys, [hq+hkv, hq+2hkv) values.
-// Rotate-half RoPE (HF apply_rotary_pos_emb) on q and k; k and v land in the token's paged slot.
+// One CTA per (token, head); thread j owns the rotate-half pair (j, j + d/2). Heads [0,hq) are
+// queries, [hq,hq+hkv) keys, [hq+hkv, hq+2hkv) values. RoPE (HF apply_rotary_pos_emb) on q and k;
+// k and v land in the token's paged slot.
 __global__ void rope_kv_append_kernel(const float* __restrict__ qkv, int64_t ld_qkv,
                                       const int32_t* __restrict__ positions, const float* __restrict__ cos_sin,
                                       int max_pos, const int32_t* __restrict__ slots, int hq, int hkv, int d,
                                       float* __restrict__ q_out, __nv_bfloat16* __restrict__ k_pool,
                                       __nv_bfloat16* __restrict__ v_pool, int64_t num_blocks) {
-  const int i = blockIdx.x;
+  griddep_launch();
+  griddep_wait();
+  const int i = blockIdx.x, hd = blockIdx.y, j = threadIdx.x;
   const int half = d >> 1;
-  const float* row = qkv + (int64_t)i * ld_qkv;
-  const float* cs = nullptr;
-  if (cos_sin) {
+  if (j >= half) return;
+  const float* src = qkv + (int64_t)i * ld_qkv + (int64_t)hd * d;
+  float a = src[j], b = src[j + half];
+  if (hd < hq + hkv && cos_sin) {
     const int pos = positions[i];
     if (pos < 0 || pos >= max_pos) {
-      if (threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 200);
+      if (j == 0) mg_record_error(MG_ERR_DEVICE, 200);
       return;
     }
-    cs = cos_sin + (int64_t)pos * d;
+    const float* cs = cos_sin + (int64_t)pos * d;
+    const float c = cs[j], s = cs[half + j];
+    const float ra = a * c - b * s;
+    const float rb = b * c + a * s;
+    a = ra;
+    b = rb;
+  }
+  if (hd < hq) {
+    float* dst = q_out + ((int64_t)i * hq + hd) * d;
+    dst[j] = a;
+    dst[j + half] = b;
+    return;
   }
   const int slot = slots[i];
   const int64_t blk = slot >> 4;
-  const int off = slot & 15;
-  const bool slot_ok = slot >= 0 && blk < num_blocks;
-  if (!slot_ok && threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 201);
-  const int nheads = hq + 2 * hkv;
-  for (int e = threadIdx.x; e < nheads * half; e += blockDim.x) {
-    const int hd = e / half, j = e % half;
-    const float* src = row + (int64_t)hd * d;
-    float a = src[j], b = src[j + half];
-    if (hd < hq + hkv && cs) {
-      const float c = cs[j], s = cs[half + j];
-      const float ra = a * c - b * s;
-      const float rb = b * c + a * s;
-      a = ra;
-      b = rb;
-    }
-    if (hd < hq) {
-      float* dst = q_out + ((int64_t)i * hq + hd) * d;
-      dst[j] = a;
-      dst[j + half] = b;
-    } else if (slot_ok) {
-      const bool is_k = hd < hq + hkv;
-      const int kh = is_k ? hd - hq : hd - hq - hkv;
-      __nv_bfloat16* pool = is_k ? k_pool : v_pool;
-      __nv_bfloat16* dst = pool + ((blk * hkv + kh) * 16 + off) * (int64_t)d;
-      dst[j] = __float2bfloat16_rn(a);
-      dst[j + half] = __float2bfloat16_rn(b);
-    }
+  if (slot < 0 || blk >= num_blocks) {
+    if (j == 0) mg_record_error(MG_ERR_DEVICE, 201);
+    return;
   }
+  const bool is_k = hd < hq + hkv;
+  const int kh = is_k ? hd - hq : hd - hq - hkv;
+  __nv_bfloat16* dst = (is_k ? k_pool : v_pool) + ((blk * hkv + kh) * 16 + (slot & 15)) * (int64_t)d;
+  dst[j] = __float2bfloat16_rn(a);
+  dst[j + half] = __float2bfloat16_rn(b);
 }
 
 // torch.argmax semantics: the first index holding the maximum.
 __global__ void argmax_kernel(const float* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ out) {
+  griddep_launch();
+  griddep_wait();
   __shared__ float sv[32];
   __shared__ int32_t si[32];
   const float* r = logits + (int64_t)blockIdx.x * ld;
@@ -203,6 +264,8 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t n, int64
 __global__ void decode_advance_kernel(int32_t* tokens, const int32_t* next_tokens, int32_t* positions,
                                       int32_t* ctx_lens, int32_t* slots, const int32_t* tables, int max_blocks,
                                       int b) {
+  griddep_launch();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= b) return;
   tokens[i] = next_tokens[i];
@@ -223,24 +286,32 @@ __global__ void decode_advance_kernel(int32_t* tokens, const int32_t* next_token
 extern "C" int mg_quantize_rows_i8(const float* w, int64_t n, int64_t k, int8_t* q, float* scales, void* stream) {
   if (n < 0 || k < 0 || (n > 0 && (!w || !q || !scales)) || n > 0x7fffffff) return MG_ERR_INVALID_ARG;
   if (n == 0) return MG_OK;
-  quantize_rows_kernel<<<(unsigned)n, kRowThreads, 0, mg_stream(stream)>>>(w, k, q, scales);
+  MG_CUDA_TRY(mg_launch(quantize_rows_kernel, dim3((unsigned)n), dim3(kRowThreads), 0, mg_stream(stream), 1, w, k, q, scales));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }
 
 extern "C" int mg_rmsnorm(const float* h, const float* w, int m, int n, float eps, void* x, void* stream) {
-  if (m < 0 || n <= 0 || !h || !w || !x) return MG_ERR_INVALID_ARG;
+  if (m < 0 || n <= 0 || n % 4 || n > 4 * kRowThreads * kNormMaxV || !h || !w || !x) return MG_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15)
+    return MG_ERR_INVALID_ARG;
   if (m == 0) return MG_OK;
-  rmsnorm_kernel<<<m, kRowThreads, 0, mg_stream(stream)>>>(h, w, n, eps, static_cast<__nv_bfloat16*>(x));
+  MG_CUDA_TRY(mg_launch(rmsnorm_kernel, dim3(m), dim3(kRowThreads), 0, mg_stream(stream), 1, h, w, n, eps,
+                        static_cast<__nv_bfloat16*>(x)));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }
 
 extern "C" int mg_layernorm(const float* h, const float* w, const float* bias, int m, int n, float eps, void* x,
                             void* stream) {
-  if (m < 0 || n <= 0 || !h || !w || !bias || !x) return MG_ERR_INVALID_ARG;
+  if (m < 0 || n <= 0 || n % 4 || n > 4 * kRowThreads * kNormMaxV || !h || !w || !bias || !x)
+    return MG_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(bias) |
+       reinterpret_cast<uintptr_t>(x)) & 15)
+    return MG_ERR_INVALID_ARG;
   if (m == 0) return MG_OK;
-  layernorm_kernel<<<m, kRowThreads, 0, mg_stream(stream)>>>(h, w, bias, n, eps, static_cast<__nv_bfloat16*>(x));
+  MG_CUDA_TRY(mg_launch(layernorm_kernel, dim3(m), dim3(kRowThreads), 0, mg_stream(stream), 1, h, w, bias, n, eps,
+                        static_cast<__nv_bfloat16*>(x)));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }
@@ -250,7 +321,8 @@ extern "C" int mg_embed(const int32_t* tokens, const int32_t* positions, const f
   if (b < 0 || hidden <= 0 || vocab <= 0 || !tokens || !wte || !h || (wpe && (!positions || max_pos <= 0)))
     return MG_ERR_INVALID_ARG;
   if (b == 0) return MG_OK;
-  embed_kernel<<<b, kRowThreads, 0, mg_stream(stream)>>>(tokens, positions, wte, wpe, hidden, vocab, max_pos, h);
+  MG_CUDA_TRY(mg_launch(embed_kernel, dim3(b), dim3(kRowThreads), 0, mg_stream(stream), 1, tokens, positions, wte, wpe,
+                        hidden, vocab, max_pos, h));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }
@@ -262,9 +334,11 @@ extern "C" int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t
       !v_pool || num_blocks <= 0 || ld_qkv < (int64_t)(hq + 2 * hkv) * d || (cos_sin && (!positions || max_pos <= 0)))
     return MG_ERR_INVALID_ARG;
   if (b == 0) return MG_OK;
-  rope_kv_append_kernel<<<b, kRowThreads, 0, mg_stream(stream)>>>(
-      qkv, ld_qkv, positions, cos_sin, max_pos, slot_mapping, hq, hkv, d, q_out,
-      static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), num_blocks);
+  if (d > 2 * 1024) return MG_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)b, (unsigned)(hq + 2 * hkv));
+  MG_CUDA_TRY(mg_launch(rope_kv_append_kernel, grid, dim3((d / 2 + 31) / 32 * 32), 0, mg_stream(stream), 1, qkv,
+                        ld_qkv, positions, cos_sin, max_pos, slot_mapping, hq, hkv, d, q_out,
+                        static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), num_blocks));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }
@@ -272,7 +346,7 @@ extern "C" int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t
 extern "C" int mg_argmax_rows(const float* logits, int m, int64_t n, int64_t ld, int32_t* out, void* stream) {
   if (m < 0 || n <= 0 || ld < n || !logits || !out || n > 0x7fffffff) return MG_ERR_INVALID_ARG;
   if (m == 0) return MG_OK;
-  argmax_kernel<<<m, 1024, 0, mg_stream(stream)>>>(logits, n, ld, out);
+  MG_CUDA_TRY(mg_launch(argmax_kernel, dim3(m), dim3(1024), 0, mg_stream(stream), 1, logits, n, ld, out));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }
@@ -282,8 +356,8 @@ extern "C" int mg_decode_advance(int32_t* tokens, const int32_t* next_tokens, in
   if (b < 0 || max_blocks <= 0 || !tokens || !next_tokens || !positions || !ctx_lens || !slots || !block_tables)
     return MG_ERR_INVALID_ARG;
   if (b == 0) return MG_OK;
-  decode_advance_kernel<<<(b + 127) / 128, 128, 0, mg_stream(stream)>>>(tokens, next_tokens, positions, ctx_lens,
-                                                                        slots, block_tables, max_blocks, b);
+  MG_CUDA_TRY(mg_launch(decode_advance_kernel, dim3((b + 127) / 128), dim3(128), 0, mg_stream(stream), 1, tokens,
+                        next_tokens, positions, ctx_lens, slots, block_tables, max_blocks, b));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }

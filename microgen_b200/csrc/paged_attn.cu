@@ -345,6 +345,8 @@ __device__ void shared_cta(const AttnParams& p, int h, int chunk, uint8_t* smem)
 template <int D>
 __global__ void __launch_bounds__(kThreads) paged_attn_kernel(const AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
+  griddep_launch();
+  griddep_wait();
   const int n_shared_ctas = p.n_shared_ctas_per_head * p.hkv;
   if ((int)blockIdx.x < n_shared_ctas) {
     shared_cta<D>(p, blockIdx.x / p.n_shared_ctas_per_head, blockIdx.x % p.n_shared_ctas_per_head, smem);
@@ -357,6 +359,8 @@ __global__ void __launch_bounds__(kThreads) paged_attn_kernel(const AttnParams p
 template <int D>
 __global__ void combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml, int nslots,
                                __nv_bfloat16* __restrict__ out) {
+  griddep_launch();
+  griddep_wait();
   const int64_t sh = blockIdx.x;  // seq * hq + head
   const int d = threadIdx.x;
   const float* ml = ws_ml + sh * nslots * 2;
@@ -416,11 +420,10 @@ int launch_attn(AttnParams& p, const Plan& pl, cudaStream_t st) {
   }
   const int64_t ctas = (int64_t)pl.n_shared_ctas_per_head * p.hkv + (int64_t)p.b * p.hkv * pl.nsplit;
   if (ctas > 0x7fffffff) return MG_ERR_UNSUPPORTED;
-  paged_attn_kernel<D><<<(unsigned)ctas, kThreads, AttnCfg<D>::kSmem, st>>>(p);
-  MG_LAUNCH_CHECK();
+  MG_CUDA_TRY(mg_launch(paged_attn_kernel<D>, dim3((unsigned)ctas), dim3(kThreads), AttnCfg<D>::kSmem, st, 1, p));
   if (!pl.direct) {
-    combine_kernel<D><<<(unsigned)(p.b * p.hq), D, 0, st>>>(p.ws_o, p.ws_ml, pl.nslots, p.out);
-    MG_LAUNCH_CHECK();
+    MG_CUDA_TRY(mg_launch(combine_kernel<D>, dim3((unsigned)(p.b * p.hq)), dim3(D), 0, st, 1, p.ws_o, p.ws_ml,
+                          pl.nslots, p.out));
   }
   return MG_OK;
 }

@@ -75,10 +75,10 @@ class ModelWeights:
 
     def int8_bytes(self) -> int:
         """Weight bytes a decode step streams: int8 codes + fp32 scales of every linear."""
-        n = self.lm_q.numel() + 4 * self.lm_s.numel()
+        n = self.lm_q.shape[0] * self.lm_q.shape[1] + 4 * self.lm_s.numel()
         for L in self.layers:
             for q, s in ((L.qkv_q, L.qkv_s), (L.o_q, L.o_s), (L.gu_q, L.gu_s), (L.d_q, L.d_s)):
-                n += q.numel() + 4 * s.numel()
+                n += q.shape[0] * q.shape[1] + 4 * s.numel()
         return n
 
 
@@ -100,8 +100,8 @@ def _interleave_gate_up(gq, gs, uq, us, gb=None, ub=None):
 class WeightLoader:
     """Quantize full fp32 matrices on the device and keep this rank's shard."""
 
-    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1):
-        self.spec, self.device, self.rank, self.world = spec, torch.device(device), rank, world
+    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1, pack: bool = True):
+        self.spec, self.device, self.rank, self.world, self.pack = spec, torch.device(device), rank, world, pack
         if spec.heads % world or spec.kv_heads % world:
             raise ValueError(f"{spec.heads} query / {spec.kv_heads} kv heads do not split over {world} ranks")
 
@@ -191,7 +191,13 @@ class WeightLoader:
             norm_w, norm_b = self.f32(state["model.norm.weight"]), None
             head = state.get("lm_head.weight", state["model.embed_tokens.weight"])
         lm_q, lm_s = self.quant(head)
-        return ModelWeights(embed=embed, wpe=wpe, norm_w=norm_w, norm_b=norm_b, lm_q=lm_q, lm_s=lm_s, layers=layers)
+        w = ModelWeights(embed=embed, wpe=wpe, norm_w=norm_w, norm_b=norm_b, lm_q=lm_q, lm_s=lm_s, layers=layers)
+        if self.pack:
+            w.lm_q = K.pack_weights(w.lm_q)
+            for L in layers:
+                for name in ("qkv_q", "o_q", "gu_q", "d_q"):
+                    setattr(L, name, K.pack_weights(getattr(L, name)))
+        return w
 
 
 def rope_table(head_dim: int, theta: float, max_pos: int) -> torch.Tensor:

@@ -44,8 +44,44 @@ def quantize_rows_i8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, s
 
 
-def _linear_args(x, q, scales, bias, y, epilogue):
+class PackedWeight:
+    """INT8 codes in the tile-packed layout (contiguous 16 KB block per 128x128 tile) with the
+    logical [n, k] shape of the row-major codes they were packed from."""
+    __slots__ = ("data", "n", "k")
+
+    def __init__(self, data: torch.Tensor, n: int, k: int) -> None:
+        self.data, self.n, self.k = data, n, k
+
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
+    @property
+    def device(self):
+        return self.data.device
+
+    def numel(self) -> int:
+        return self.data.numel()
+
+    def element_size(self) -> int:
+        return 1
+
+
+def packed_bytes(n: int, k: int) -> int:
+    return int(_lib.load().mg_i8_packed_bytes(n, k))
+
+
+def pack_weights(q: torch.Tensor) -> PackedWeight:
+    """Row-major int8 codes [n, k] -> tile-packed layout (see include/microgen_b200.h)."""
     _need(q, torch.int8, "q")
+    n, k = q.shape
+    data = torch.empty(packed_bytes(n, k), dtype=torch.int8, device=q.device)
+    _lib.call("mg_i8_pack_weights", _ptr(q), n, k, _ptr(data), _stream())
+    return PackedWeight(data, n, k)
+
+
+def _linear_args(x, q, scales, bias, y, epilogue):
+    _need(q.data if isinstance(q, PackedWeight) else q, torch.int8, "q")
     _need(scales, torch.float32, "scales")
     if bias is not None:
         _need(bias, torch.float32, "bias")
@@ -68,8 +104,13 @@ def _linear_args(x, q, scales, bias, y, epilogue):
 
 
 def i8_linear(x, q, scales, bias=None, y=None, epilogue=EPI_STORE_BF16, algo: str = "auto", split_k: int = 0):
-    """y = epilogue(x · (q·s)ᵀ + bias); returns y. algo: "auto" | "tc" | "simt"."""
+    """y = epilogue(x · (q·s)ᵀ + bias); returns y. algo: "auto" | "tc" | "simt" (row-major q);
+    a PackedWeight q runs the tensor-core kernel on tile-packed codes."""
     m, k, n, y = _linear_args(x, q, scales, bias, y, epilogue)
+    if isinstance(q, PackedWeight):
+        _lib.call("mg_i8_linear_packed", _ptr(x), m, k, x.stride(0), _ptr(q.data), _ptr(scales), _ptr(bias), n,
+                  _ptr(y), y.stride(0), int(epilogue), int(split_k), _stream())
+        return y
     args = (_ptr(x), m, k, x.stride(0), _ptr(q), _ptr(scales), _ptr(bias), n, _ptr(y), y.stride(0), int(epilogue))
     if algo == "simt":
         _lib.call("mg_i8_linear_simt", *args, _stream())

@@ -260,3 +260,40 @@ def test_paged_attention_shared_prefix_equals_unshared():
 
 def test_no_device_error_recorded():
     K().check_device()
+
+
+# ------------------------------------------------------------------ tile-packed weights
+@pytest.mark.parametrize("n,k", [(384, 256), (200, 96), (1000, 3072), (3072, 448)])
+def test_pack_layout(n, k):
+    rng = np.random.default_rng(n + k)
+    q = rng.integers(-128, 128, size=(n, k), dtype=np.int8)
+    pw = K().pack_weights(dev(q))
+    tiles, kb = (n + 127) // 128, (k + 127) // 128
+    ref = np.zeros((tiles * 128, kb * 128), np.int8)
+    ref[:n, :k] = q
+    ref = ref.reshape(tiles, 128, kb, 128).transpose(0, 2, 1, 3).reshape(-1)
+    assert np.array_equal(pw.data.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("m,k,n,split", [(1, 3072, 640, 0), (32, 3072, 1024, 0), (32, 448, 896, 3),
+                                         (100, 1024, 640, 2), (256, 512, 256, 0), (7, 96, 200, 1)])
+def test_packed_linear_vs_oracle_and_rowmajor(m, k, n, split):
+    x, q, s, b = _mk_linear(m, k, n, seed=m * 3 + k + n)
+    k_ = K()
+    xd, qd, sd, bd = dev(x, torch.bfloat16), dev(q), dev(s), dev(b)
+    pw = k_.pack_weights(qd)
+    y = k_.i8_linear(xd, pw, sd, bd, epilogue=k_.EPI_STORE_F32, split_k=split)
+    close(y.cpu().numpy(), olin.i8_linear(x, q, s, b), rtol=1e-4, atol=1e-4)
+    y_rm = k_.i8_linear(xd, qd, sd, bd, epilogue=k_.EPI_STORE_F32, algo="tc", split_k=split)
+    if split:
+        assert torch.equal(y, y_rm)  # same tiles, same split: identical sums
+
+
+def test_packed_linear_swiglu_epilogue():
+    k_ = K()
+    m, k, n = 32, 768, 512
+    x, q, s, b = _mk_linear(m, k, n, seed=77)
+    want = olin.i8_linear(x, q, s, b).reshape(m, n // 128, 2, 64)
+    gate, up = want[:, :, 0, :].reshape(m, -1), want[:, :, 1, :].reshape(m, -1)
+    sw = k_.i8_linear(dev(x, torch.bfloat16), k_.pack_weights(dev(q)), dev(s), dev(b), epilogue=k_.EPI_SWIGLU_BF16)
+    close(sw.float().cpu().numpy(), gate / (1 + np.exp(-gate)) * up)

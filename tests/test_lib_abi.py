@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "microgen_b200.h")
 def declared_symbols() -> list[str]:
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(mg_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(mg_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")
