@@ -104,6 +104,24 @@ int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool,
                          int hkv, int d, int n_shared_blocks, float scale, void* out, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Allocation-free paged decode attention. No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory themselves — a host binding that only receives pointers from another
+ * runtime's allocator, or a serving loop that must not take cudaMalloc's device-wide synchronisation in
+ * the middle of a step. Same contract as mg_paged_decode_attn, but the split scratch is a fixed
+ * library-owned device array of MG_ATTN_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps
+ * until the process exits; the caller still passes q, the pools, the tables, ctx_lens and `out`.
+ * Limit: returns MG_ERR_UNSUPPORTED when mg_paged_attn_workspace_bytes() for the sizes exceeds the array.
+ * Allocates nothing (no cudaMalloc / cudaFree / allocating library call). The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress, once per device, with that device current);
+ * make that first call before any stream capture. All calls share the array: calls whose kernels
+ * overlap on the GPU (e.g. on two streams) race on it — serialise them. Nothing in it needs clearing:
+ * each call writes every slot it later reads. */
+#define MG_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
+int mg_paged_decode_attn_noalloc(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                 const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,
+                                 int hq, int hkv, int d, int n_shared_blocks, float scale, void* out,
+                                 void* stream);
+
 /* ---- small fused ops of the decode step ---------------------------------------------------- */
 /* h fp32 [b, hidden] = wte[tokens[i]] (+ wpe[positions[i]] when wpe != NULL). */
 int mg_embed(const int32_t* tokens, const int32_t* positions, const float* wte, const float* wpe, int b,

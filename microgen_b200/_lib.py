@@ -43,6 +43,7 @@ SIGNATURES = {
     "mg_rope_kv_append": [_p, _i64, _p, _p, _i, _p, _i, _i, _i, _i, _p, _p, _p, _i64, _p],
     "mg_paged_attn_workspace_bytes": [_i, _i, _i, _i, _i, _i, C.POINTER(C.c_size_t)],
     "mg_paged_decode_attn": [_p, _p, _p, _i64, _p, _i, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p],
+    "mg_paged_decode_attn_noalloc": [_p, _p, _p, _i64, _p, _i, _p, _i, _i, _i, _i, _i, _f, _p, _p],
     "mg_embed": [_p, _p, _p, _p, _i, _i, _i64, _i, _p, _p],
     "mg_rmsnorm": [_p, _p, _i, _i, _f, _p, _p],
     "mg_layernorm": [_p, _p, _p, _i, _i, _f, _p, _p],
@@ -53,7 +54,7 @@ _RESTYPES = {"mg_status_string": C.c_char_p, "mg_i8_packed_bytes": C.c_int64}
 
 # entry points that launch one kernel per call (mg_paged_decode_attn adds its combine kernel)
 LAUNCHING = {"mg_quantize_rows_i8", "mg_i8_linear", "mg_i8_linear_simt", "mg_i8_linear_tc", "mg_rope_kv_append",
-             "mg_i8_pack_weights", "mg_i8_linear_packed",
+             "mg_i8_pack_weights", "mg_i8_linear_packed", "mg_paged_decode_attn_noalloc",
              "mg_paged_decode_attn", "mg_embed", "mg_rmsnorm", "mg_layernorm", "mg_argmax_rows",
              "mg_decode_advance"}
 LAUNCHES = [0]  # kernels launched (or captured) through call() in this process

@@ -480,3 +480,53 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
   if (d == 32) return launch_attn<32>(p, pl, st);
   return d == 64 ? launch_attn<64>(p, pl, st) : launch_attn<128>(p, pl, st);
 }
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free variant: the split scratch lives in a file-scope device array.
+// ------------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+// Every GPU that loads this library holds this array until the process exits.
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[MG_ATTN_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoAllocMaxDevices = 64;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device. In host code the array's name is only a
+// host-side stand-in, so the address is looked up once per device (with that device current) and kept.
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  MG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return MG_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    MG_CUDA_TRY(cudaGetSymbolAddress(&p, g_attn_noalloc_scratch));
+    if (!p) return MG_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return MG_OK;
+}
+
+}  // namespace
+
+extern "C" int mg_paged_decode_attn_noalloc(const float* q, const void* k_pool, const void* v_pool,
+                                            int64_t num_blocks, const int32_t* block_tables, int max_blocks,
+                                            const int32_t* ctx_lens, int b, int hq, int hkv, int d,
+                                            int n_shared_blocks, float scale, void* out, void* stream) {
+  size_t need = 0;
+  int rc = mg_paged_attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks, &need);
+  if (rc) return rc;
+  if (need > (size_t)MG_ATTN_NOALLOC_SCRATCH_BYTES) return MG_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(&scratch);
+  if (rc) return rc;
+  // Every split slot the combine step reads is written by this call's attention CTAs first, so the
+  // previous call's contents never need clearing.
+  return mg_paged_decode_attn(q, k_pool, v_pool, num_blocks, block_tables, max_blocks, ctx_lens, b, hq, hkv, d,
+                              n_shared_blocks, scale, out, scratch, (size_t)MG_ATTN_NOALLOC_SCRATCH_BYTES, stream);
+}
