@@ -150,6 +150,14 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+T0 = time.time()
+
+
+def log(msg: str) -> None:
+    """Progress line on stderr (rank-tagged), so a stalled run shows its phase."""
+    print(f"[bench r{os.environ.get('RANK', '0')} +{time.time() - T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def random_fill(be, prompts, n_shared):
     """Profile mode: block tables as a prefill would leave them (shared prefix by reference
     count), the KV pool filled with seeded random bf16 values instead of computed K/V."""
@@ -214,6 +222,7 @@ def main():
     be = (B200TensorParallelBackend(world_size=world, group=group, **kw) if world > 1
           else B200QuantizedBackend(**kw))
     t0 = time.time()
+    log(f"loading {wl['shape']} tp={world}")
     be.load_state(spec, SyntheticState(spec, seed=0, device=torch.device("cuda", local)))
     torch.cuda.synchronize()
     t_load = time.time() - t0
@@ -224,6 +233,7 @@ def main():
     prompts = torch.stack([torch.cat([shared, torch.randint(0, spec.vocab, (P - S,), generator=g)])
                            for _ in range(B)])
     t0 = time.time()
+    log("prefill")
     if args.profile:
         cache = random_fill(be, prompts, n_shared)
         first = prompts[:, -1].to(torch.int32)
@@ -233,6 +243,7 @@ def main():
     torch.cuda.synchronize()
     t_prefill = time.time() - t0
 
+    log("decode: capture + timed replays")
     # ---- device-timed decode: graph replays, inputs resident, device-side advance --------------
     alloc = be.allocator
     for t in cache.tables:
@@ -279,6 +290,7 @@ def main():
     kv_tokens = n_shared * 16 + B * (int(mean_pos) + 1 - n_shared * 16)
 
     if args.profile:
+        del graph  # a graph holding NCCL calls must be gone before the process group is destroyed
         eng.release_graphs()
         if rank == 0:
             print(json.dumps({"profile": args.workload, "ms_per_step": round(ms, 4), "value": round(value, 1)}))
@@ -304,6 +316,7 @@ def main():
             self.b.record(torch.cuda.current_stream())
             stats.setdefault(self.kind, []).append((self.a, self.b, self.nbytes))
 
+    log("per-kernel probe")
     pos = int(mean_pos)
     eng.set_inputs(first.tolist(), [pos] * B, [t.slot(pos) for t in cache.tables], [pos + 1] * B, tab)
     for rep in range(4):
@@ -337,6 +350,7 @@ def main():
 
     # ---- end to end through the public API (host ids in, host ids out) -------------------------
     e2e = None
+    log("e2e")
     if not args.no_e2e:
         for t in cache.tables:
             alloc.rollback(t, t.num_tokens - (P + skip))
@@ -364,10 +378,15 @@ def main():
     K.check_device()
 
     cpu = None
+    log("cpu baseline / report")
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(spec, wl, P + Dec // 2, budget_s=20.0)
 
+    del graph  # a graph holding NCCL calls must be gone before the process group is destroyed
     eng.release_graphs()
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

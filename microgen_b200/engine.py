@@ -97,11 +97,27 @@ def _interleave_gate_up(gq, gs, uq, us, gb=None, ub=None):
     return q, s, b
 
 
-class WeightLoader:
-    """Quantize full fp32 matrices on the device and keep this rank's shard."""
+def row_parallel_residual(h: torch.Tensor, launch, rank: int, world: int, group=None) -> None:
+    """Row-parallel linear folded into the fp32 residual ``h`` (replicated on every rank).
 
-    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1, pack: bool = True):
+    ``launch(y, epilogue)`` runs this rank's partial linear into ``y`` with the given epilogue.
+    Rank 0 adds its partial (and the bias) into ``h`` in place; every other rank overwrites its copy of
+    ``h`` with its partial; one in-place sum all-reduce then leaves ``h + Σ partials`` on every rank —
+    the reference's ``sum(partial_outputs) + bias`` (``parallel.py:65-81``) added to the residual."""
+    launch(h, K.EPI_ADD_F32 if rank == 0 else K.EPI_STORE_F32)
+    if world > 1:
+        torch.distributed.all_reduce(h, group=group)
+
+
+class WeightLoader:
+    """Quantize full fp32 matrices on the device and keep this rank's shard.
+
+    ``quantize`` maps an fp32 [N, K] weight to (int8 codes, fp32 scales) — the bit-exact device kernel
+    by default; ``pack`` repacks the kept codes into the tile-packed layout."""
+
+    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1, pack: bool = True, quantize=None):
         self.spec, self.device, self.rank, self.world, self.pack = spec, torch.device(device), rank, world, pack
+        self.quantize = quantize or K.quantize_rows_i8
         if spec.heads % world or spec.kv_heads % world:
             raise ValueError(f"{spec.heads} query / {spec.kv_heads} kv heads do not split over {world} ranks")
 
@@ -109,7 +125,7 @@ class WeightLoader:
         return t.detach().to(device=self.device, dtype=torch.float32).contiguous()
 
     def quant(self, w_out_in) -> tuple[torch.Tensor, torch.Tensor]:
-        return K.quantize_rows_i8(self.f32(w_out_in))
+        return self.quantize(self.f32(w_out_in))
 
     def rows(self, t, n_total):
         per = n_total // self.world
@@ -256,10 +272,6 @@ class DecodeEngine:
         else:
             K.rmsnorm(h, w, self.spec.eps, x=x)
 
-    def _allreduce(self, t):
-        if self.world > 1:
-            torch.distributed.all_reduce(t, group=self.group)
-
     @staticmethod
     def linear_bytes(q: torch.Tensor, m: int, out_bytes: int, n_out: int) -> int:
         """Algorithmic bytes of one INT8 linear launch: codes + scales + x (bf16) + y."""
@@ -277,7 +289,6 @@ class DecodeEngine:
         s, w = self.spec, self.w
         h, x = self.h[:b], self.x[:b]
         tab, ctx = self.tables[:b], self.ctx[:b]
-        epi_res = K.EPI_ADD_F32 if self.rank == 0 else K.EPI_STORE_F32
         P = probe if probe is not None else (lambda kind, nbytes: contextlib.nullcontext())
         H, D = s.hidden, self.D
         nqkv = (self.hq + 2 * self.hkv) * D
@@ -296,16 +307,16 @@ class DecodeEngine:
                 K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
                                     n_shared_blocks=n_shared_blocks, out=self.attn[:b], workspace=self.workspace)
             with P("i8_linear", self.linear_bytes(L.o_q, b, 8, H)):
-                K.i8_linear(self.attn[:b], L.o_q, L.o_s, L.o_b, y=h, epilogue=epi_res)
-            self._allreduce(h)
+                row_parallel_residual(h, lambda y, e: K.i8_linear(self.attn[:b], L.o_q, L.o_s, L.o_b, y=y, epilogue=e),
+                                      self.rank, self.world, self.group)
             with P("norm", b * H * 6):
                 self._norm(h, L.ln2_w, L.ln2_b, x)
             epi_mlp = K.EPI_GELU_BF16 if s.family == "gpt2" else K.EPI_SWIGLU_BF16
             with P("i8_linear", self.linear_bytes(L.gu_q, b, 2, self.act.shape[1])):
                 K.i8_linear(x, L.gu_q, L.gu_s, L.gu_b, y=self.act[:b], epilogue=epi_mlp)
             with P("i8_linear", self.linear_bytes(L.d_q, b, 8, H)):
-                K.i8_linear(self.act[:b], L.d_q, L.d_s, L.d_b, y=h, epilogue=epi_res)
-            self._allreduce(h)
+                row_parallel_residual(h, lambda y, e: K.i8_linear(self.act[:b], L.d_q, L.d_s, L.d_b, y=y, epilogue=e),
+                                      self.rank, self.world, self.group)
         if compute_logits:
             with P("norm", b * H * 6):
                 self._norm(h, w.norm_w, w.norm_b, x)

@@ -1,0 +1,86 @@
+"""Tensor parallelism across real GPUs (needs >= 2): TP=2 decode through B200TensorParallelBackend,
+one process per GPU over NCCL, against TP=1 on the same seeded model. TP=2 is teacher-forced with the
+TP=1 greedy stream: logits must agree within the bf16 tolerance at every step, and the argmax must agree
+wherever TP=1's top-1/top-2 margin exceeds that tolerance (TP sums the row-parallel partials in another
+order, so only near-ties may flip). Skipped when fewer than two GPUs are visible."""
+
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SHAPE = dict(family="llama", hidden=512, layers=2, heads=8, kv_heads=4, head_dim=64, inter=1024, vocab=1024,
+             eps=1e-5, rope_theta=500000.0)
+N_NEW = 24
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _decode(be, prompts, forced=None):
+    """Greedy decode (or, with ``forced``, feed those tokens); returns (tokens, logits per step)."""
+    logits, cache = be.prefill(torch.tensor(prompts))
+    toks, lgs = [], [logits.float().cpu().numpy()]
+    for i in range(N_NEW):
+        t = be.sample(logits) if forced is None else torch.tensor(forced[i], device="cuda")[:, None]
+        toks.append(t[:, 0].cpu().tolist())
+        logits, cache = be.decode(t, cache=cache)
+        lgs.append(logits.float().cpu().numpy())
+    return toks, np.stack(lgs)
+
+
+def _prompts():
+    from tests._hf_models import prompt_ids
+    shared = prompt_ids(SHAPE["vocab"], 32, seed=7)
+    return [shared + prompt_ids(SHAPE["vocab"], 9, seed=20 + i) for i in range(4)]
+
+
+def _worker(rank, world, port, outdir, graph, forced):
+    import torch.distributed as dist
+    from microgen_b200.backends import B200TensorParallelBackend
+    from tests._hf_models import make_hf_model
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    model, _ = make_hf_model(SHAPE, seed=0)
+    be = B200TensorParallelBackend(world_size=world, group=dist.group.WORLD, max_batch=4, max_seq_len=128,
+                                   use_cuda_graph=graph, free_list_seed=1)
+    be.load_model("tiny", model_instance=model)
+    out = _decode(be, _prompts(), forced)
+    be.engine.release_graphs()
+    torch.save(out, os.path.join(outdir, f"r{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("graph", [False, True])
+def test_tp2_matches_tp1(graph):
+    import torch.multiprocessing as mp
+    from microgen_b200.backends import B200QuantizedBackend
+    from tests._hf_models import make_hf_model
+    model, _ = make_hf_model(SHAPE, seed=0)
+    be = B200QuantizedBackend(max_batch=4, max_seq_len=128, free_list_seed=1, use_cuda_graph=graph)
+    be.load_model("tiny", model_instance=model)
+    ref_toks, ref_lg = _decode(be, _prompts())
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks), nprocs=2, join=True)
+        outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(2)]
+    tol = 1e-2 + 2e-2 * np.abs(ref_lg)
+    top2 = np.sort(ref_lg, axis=-1)[..., -2:]
+    clear = (top2[..., 1] - top2[..., 0]) > 2 * tol.max(axis=-1)
+    for toks, lg in outs:
+        assert toks == ref_toks  # teacher-forced inputs
+        err = np.abs(lg - ref_lg)
+        assert not (err > tol).any(), f"max err {err.max():.3e}"
+        agree = np.argmax(lg, axis=-1) == np.argmax(ref_lg, axis=-1)
+        assert agree[clear].all()
+        assert clear.mean() > 0.3  # enough clear-margin steps for the argmax check to mean something
