@@ -227,6 +227,8 @@ def main():
     torch.cuda.synchronize()
     t_load = time.time() - t0
     eng = be.engine
+    reduce_kind = ("fused peer-memory push" if eng.comm is not None else
+                   ("nccl all_reduce" if world > 1 else "none (tp1)"))
 
     g = torch.Generator().manual_seed(1)
     shared = torch.randint(0, spec.vocab, (S,), generator=g)
@@ -295,6 +297,10 @@ def main():
         if rank == 0:
             print(json.dumps({"profile": args.workload, "ms_per_step": round(ms, 4), "value": round(value, 1)}))
         if world > 1:
+            torch.cuda.synchronize()
+            dist.barrier()
+            eng.close()
+            dist.barrier()
             dist.destroy_process_group()
         return
 
@@ -389,6 +395,8 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+        eng.close()  # peers are done writing into this rank's receive area
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -399,7 +407,8 @@ def main():
         "config": {"workload": f"{args.workload}: {wl['shape']} INT8, batch {B}, prompt {P} ({S} shared), decode "
                                f"{Dec}; timed window mean ctx {mean_pos + 1:.0f}",
                    "batch": B, "prompt": P, "shared_prefix": S, "tp": world, "parallelism": f"tp{world}",
-                   "l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True},
+                   "l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True,
+                   "row_parallel_reduce": reduce_kind},
         "roofline": roofline, "step_roofline": step_roofline, "kernels": kernels,
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst,
         "clocks": clk.summary(), "setup_s": {"load": round(t_load, 1), "prefill": round(t_prefill, 1)},

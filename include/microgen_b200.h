@@ -12,7 +12,8 @@
  *   microgen/backends/quantized.py:30-39   quantize_linear_layer_per_channel -> mg_quantize_rows_i8
  *   microgen/backends/quantized.py:24-27   QuantizedLinear.forward           -> mg_i8_linear
  *   microgen/backends/parallel.py:34-37    ColumnParallelLinear.forward      -> mg_i8_linear on the rank's shard
- *   microgen/backends/parallel.py:65-81    RowParallelLinear.forward (+sum)  -> mg_i8_linear + mg_allreduce_*
+ *   microgen/backends/parallel.py:65-81    RowParallelLinear.forward (+sum)  -> mg_i8_linear_packed_rowpar +
+ *                                                                            mg_rowpar_reduce_norm
  *   microgen/runtime/kv_cache.py:76-127    KVCacheState.update (torch.cat)   -> mg_rope_kv_append (paged slot write)
  *   transformers sdpa_attention_forward    decode SDPA over the cache        -> mg_paged_decode_attn
  *   microgen/backends/pytorch.py:153-155   greedy torch.argmax               -> mg_argmax_rows
@@ -80,6 +81,27 @@ int mg_i8_pack_weights(const int8_t* q, int64_t n, int64_t k, int8_t* packed, vo
 /* mg_i8_linear_tc on tile-packed codes (same contract otherwise; split_k 0 = automatic). */
 int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed, const float* scales,
                         const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, int split_k, void* stream);
+
+/* ---- fused row-parallel all-reduce over peer memory (parallel.py:65-81 + its "all-reduce") ---------
+ * One communicator per rank of a tensor-parallel group (world <= 8, one process per GPU):
+ *   mg_comm_create  allocates this rank's receive area (2 sets x world x slot_elems fp32 + flags) and
+ *                   writes its CUDA IPC handle (mg_comm_handle_bytes() bytes) to ipc_handle;
+ *   mg_comm_open    maps every rank's area from the world handles (rank order, concatenated);
+ *   mg_comm_destroy unmaps and frees.
+ * mg_i8_linear_packed_rowpar runs this rank's partial of a row-parallel linear (tile-packed codes, scale
+ * applied, no bias) and its epilogue stores each output tile straight into every rank's receive slot over
+ * NVLink, then publishes a per-rank flag. mg_rowpar_reduce_norm waits (at most about 1 s, then
+ * MG_ERR_TIMEOUT in the device error word) for every rank's flag, sets h += sum over ranks (rank order) +
+ * bias, and with norm = 1 (RMSNorm, w) or 2 (LayerNorm, w, wb) writes x = bf16(norm(h)). Every rank must
+ * issue the same sequence of rowpar / reduce calls. m * n <= slot_elems. */
+int mg_comm_handle_bytes(void);
+int mg_comm_create(int rank, int world, int64_t slot_elems, void** comm, void* ipc_handle);
+int mg_comm_open(void* comm, const void* ipc_handles);
+int mg_comm_destroy(void* comm);
+int mg_i8_linear_packed_rowpar(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                               const float* scales, int64_t n, void* comm, int split_k, void* stream);
+int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, int m, int n, int norm, const float* w,
+                          const float* wb, float eps, void* x, void* stream);
 
 /* ---- paged KV: RoPE + append (kv_cache.py:76-127, as one slot write per token) ------------ */
 /* qkv fp32 [b, (hq+2*hkv)*d] (row stride ld_qkv): q heads, then k heads, then v heads.

@@ -40,6 +40,12 @@ SIGNATURES = {
     "mg_i8_packed_bytes": [_i64, _i64],
     "mg_i8_pack_weights": [_p, _i64, _i64, _p, _p],
     "mg_i8_linear_packed": [_p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _i, _p],
+    "mg_comm_handle_bytes": [],
+    "mg_comm_create": [_i, _i, _i64, C.POINTER(C.c_void_p), _p],
+    "mg_comm_open": [_p, _p],
+    "mg_comm_destroy": [_p],
+    "mg_i8_linear_packed_rowpar": [_p, _i64, _i64, _i64, _p, _p, _i64, _p, _i, _p],
+    "mg_rowpar_reduce_norm": [_p, _p, _p, _i, _i, _i, _p, _p, _f, _p, _p],
     "mg_rope_kv_append": [_p, _i64, _p, _p, _i, _p, _i, _i, _i, _i, _p, _p, _p, _i64, _p],
     "mg_paged_attn_workspace_bytes": [_i, _i, _i, _i, _i, _i, C.POINTER(C.c_size_t)],
     "mg_paged_decode_attn": [_p, _p, _p, _i64, _p, _i, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p],
@@ -55,6 +61,7 @@ _RESTYPES = {"mg_status_string": C.c_char_p, "mg_i8_packed_bytes": C.c_int64}
 # entry points that launch one kernel per call (mg_paged_decode_attn adds its combine kernel)
 LAUNCHING = {"mg_quantize_rows_i8", "mg_i8_linear", "mg_i8_linear_simt", "mg_i8_linear_tc", "mg_rope_kv_append",
              "mg_i8_pack_weights", "mg_i8_linear_packed", "mg_paged_decode_attn_noalloc",
+             "mg_i8_linear_packed_rowpar", "mg_rowpar_reduce_norm",
              "mg_paged_decode_attn", "mg_embed", "mg_rmsnorm", "mg_layernorm", "mg_argmax_rows",
              "mg_decode_advance"}
 LAUNCHES = [0]  # kernels launched (or captured) through call() in this process

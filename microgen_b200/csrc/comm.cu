@@ -1,0 +1,248 @@
+// Peer-memory communicator and the reduce(+norm) half of the fused row-parallel all-reduce.
+//
+// The push half lives in the tcgen05 linear's MG_EPI_PEER_F32 epilogue (i8_linear.cu): every CTA
+// stores its output tile (scale applied, no bias) into slot [e%2][my rank] of every rank's receive
+// area over NVLink as 64-bit words {fp32 value, epoch e}; the last CTA of the launch advances this
+// rank's count to e.
+//
+// rowpar_reduce_norm_kernel reads e from the count, waits (bounded by time) until each word it
+// needs carries epoch e, sums the world partials in rank order onto the fp32 residual (identical
+// bits on every rank), adds the bias once, and applies the next RMSNorm / LayerNorm, writing bf16
+// activations for the next linear. No fences and no separate flags are involved: each word is its
+// own flag.
+//
+// Reuse of a set is safe without extra handshakes: a rank pushes e+2 only after its reduce e+1 saw
+// every peer's words of e+1, and a peer pushes e+1 only after its own reduce e consumed set e%2.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxV = 8;                     // float4 per thread: rows up to 8192
+constexpr uint64_t kWaitNs = 1000000000ull;  // a peer that has not pushed within 1 s is reported
+
+struct Comm {
+  int rank = 0, world = 1, device = 0;
+  int64_t slot = 0;
+  size_t recv_bytes = 0, bytes = 0;
+  char* base = nullptr;
+  cudaIpcMemHandle_t handle{};
+  char* peer[MG_MAX_RANKS] = {};
+  bool opened[MG_MAX_RANKS] = {};
+  bool ready = false;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+  if (w == 0) r = warp_sum(r);
+  if (threadIdx.x == 0) red[0] = r;
+  __syncthreads();
+  return red[0];
+}
+
+// Waits until the four words at p carry `epoch` (16-byte aligned). Gives up once `dead` is set or
+// the wait has run for kWaitNs, recording MG_ERR_TIMEOUT with the peer rank in the detail.
+__device__ __forceinline__ void wait_words(const uint64_t* p, uint32_t epoch, uint64_t (&wd)[4], uint64_t& t0,
+                                           bool& dead, int r) {
+  for (uint32_t spin = 0;; ++spin) {
+    ld_volatile_v2u64(p, wd[0], wd[1]);
+    ld_volatile_v2u64(p + 2, wd[2], wd[3]);
+    if (dead || ((uint32_t)(wd[0] >> 32) == epoch && (uint32_t)(wd[1] >> 32) == epoch &&
+                 (uint32_t)(wd[2] >> 32) == epoch && (uint32_t)(wd[3] >> 32) == epoch))
+      return;
+    if ((spin & 31) == 31) {
+      const uint64_t t = global_ns();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > kWaitNs) {
+        mg_record_error(MG_ERR_TIMEOUT, 600 + r);
+        dead = true;
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+// One CTA per token row. norm: 0 = none, 1 = RMSNorm (w), 2 = LayerNorm (w, wb).
+__global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po, float* __restrict__ h,
+                                                                       const float* __restrict__ bias, int n,
+                                                                       int norm, const float* __restrict__ w,
+                                                                       const float* __restrict__ wb, float eps,
+                                                                       __nv_bfloat16* __restrict__ x) {
+  __shared__ float red[32];
+  griddep_launch();
+  griddep_wait();
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(po.count);
+  const int64_t row = blockIdx.x;
+  const uint64_t* recv = po.recv[po.rank] + (int64_t)(epoch & 1u) * po.world * po.slot + row * n;
+  float* hr = h + row * n;
+  const int nv = n >> 2;
+  uint64_t t0 = 0;
+  bool dead = false;
+  float4 v[kMaxV];
+  float s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxV; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nv) {
+      float4 a = reinterpret_cast<const float4*>(hr)[idx];
+      for (int r = 0; r < po.world; ++r) {
+        uint64_t wd[4];
+        wait_words(recv + (int64_t)r * po.slot + idx * 4, epoch, wd, t0, dead, r);
+        a.x += __uint_as_float((uint32_t)wd[0]);
+        a.y += __uint_as_float((uint32_t)wd[1]);
+        a.z += __uint_as_float((uint32_t)wd[2]);
+        a.w += __uint_as_float((uint32_t)wd[3]);
+      }
+      if (bias) {
+        const float4 b = reinterpret_cast<const float4*>(bias)[idx];
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+      }
+      reinterpret_cast<float4*>(hr)[idx] = a;
+      v[i] = a;
+      s1 += norm == 2 ? (a.x + a.y + a.z + a.w) : (a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w);
+    }
+  }
+  if (norm == 0) return;
+  float mean = 0.f, inv;
+  if (norm == 1) {
+    inv = rsqrtf(block_sum(s1, red) / (float)n + eps);
+  } else {
+    mean = block_sum(s1, red) / (float)n;
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxV; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        s2 += a * a + b * b + c * c + d * d;
+      }
+    }
+    inv = rsqrtf(block_sum(s2, red) / (float)n + eps);
+  }
+  __nv_bfloat16* xr = x + row * n;
+#pragma unroll
+  for (int i = 0; i < kMaxV; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < nv) {
+      const float4 g = reinterpret_cast<const float4*>(w)[idx];
+      float4 o;
+      if (norm == 1) {
+        o = make_float4(g.x * (v[i].x * inv), g.y * (v[i].y * inv), g.z * (v[i].z * inv), g.w * (v[i].w * inv));
+      } else {
+        const float4 b = reinterpret_cast<const float4*>(wb)[idx];
+        o = make_float4((v[i].x - mean) * inv * g.x + b.x, (v[i].y - mean) * inv * g.y + b.y,
+                        (v[i].z - mean) * inv * g.z + b.z, (v[i].w - mean) * inv * g.w + b.w);
+      }
+      uint2 u;
+      u.x = pack_bf16x2(o.x, o.y);
+      u.y = pack_bf16x2(o.z, o.w);
+      reinterpret_cast<uint2*>(xr)[idx] = u;
+    }
+  }
+}
+
+}  // namespace
+
+int mg_comm_peer_out(void* comm, PeerOut* out) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || !out || !c->ready) return MG_ERR_INVALID_ARG;
+  PeerOut po{};
+  for (int r = 0; r < c->world; ++r) po.recv[r] = reinterpret_cast<uint64_t*>(c->peer[r]);
+  po.count = reinterpret_cast<uint32_t*>(c->base + c->recv_bytes);
+  po.done = po.count + 1;
+  po.slot = c->slot;
+  po.rank = c->rank;
+  po.world = c->world;
+  *out = po;
+  return MG_OK;
+}
+
+extern "C" int mg_comm_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int mg_comm_create(int rank, int world, int64_t slot_elems, void** comm, void* ipc_handle) {
+  if (!comm || !ipc_handle || world < 1 || world > MG_MAX_RANKS || rank < 0 || rank >= world || slot_elems <= 0)
+    return MG_ERR_INVALID_ARG;
+  Comm* c = new Comm();
+  c->rank = rank;
+  c->world = world;
+  c->slot = (slot_elems + 63) / 64 * 64;
+  c->recv_bytes = align_up((size_t)2 * world * c->slot * sizeof(uint64_t), 256);
+  c->bytes = c->recv_bytes + 256;  // + the two local counters
+  cudaError_t e = cudaGetDevice(&c->device);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->base), c->bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->handle, c->base);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (c->base) cudaFree(c->base);
+    delete c;
+    return mg_set_cuda_error(e);
+  }
+  std::memcpy(ipc_handle, &c->handle, sizeof(cudaIpcMemHandle_t));
+  *comm = c;
+  return MG_OK;
+}
+
+extern "C" int mg_comm_open(void* comm, const void* ipc_handles) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || !ipc_handles || c->ready) return MG_ERR_INVALID_ARG;
+  const char* hs = static_cast<const char*>(ipc_handles);
+  for (int r = 0; r < c->world; ++r) {
+    const char* h = hs + (size_t)r * sizeof(cudaIpcMemHandle_t);
+    if (r == c->rank || std::memcmp(h, &c->handle, sizeof(cudaIpcMemHandle_t)) == 0) {
+      c->peer[r] = c->base;  // this rank's own area (a handle of this process maps to itself)
+      continue;
+    }
+    cudaIpcMemHandle_t ph;
+    std::memcpy(&ph, h, sizeof(ph));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, ph, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return mg_set_cuda_error(e);
+    c->peer[r] = static_cast<char*>(p);
+    c->opened[r] = true;
+  }
+  c->ready = true;
+  return MG_OK;
+}
+
+extern "C" int mg_comm_destroy(void* comm) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c) return MG_ERR_INVALID_ARG;
+  int rc = MG_OK;
+  for (int r = 0; r < c->world; ++r)
+    if (c->opened[r] && cudaIpcCloseMemHandle(c->peer[r]) != cudaSuccess) rc = MG_ERR_CUDA;
+  if (c->base && cudaFree(c->base) != cudaSuccess) rc = MG_ERR_CUDA;
+  delete c;
+  return rc;
+}
+
+extern "C" int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, int m, int n, int norm,
+                                     const float* w, const float* wb, float eps, void* x, void* stream) {
+  PeerOut po;
+  int rc = mg_comm_peer_out(comm, &po);
+  if (rc) return rc;
+  if (!h || m < 0 || n <= 0 || n % 4 || n > 4 * kThreads * kMaxV || (int64_t)m * n > po.slot || norm < 0 ||
+      norm > 2 || (norm && (!w || !x)) || (norm == 2 && !wb))
+    return MG_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(wb) | reinterpret_cast<uintptr_t>(x)) & 15)
+    return MG_ERR_INVALID_ARG;
+  if (m == 0) return MG_OK;
+  MG_CUDA_TRY(mg_launch(rowpar_reduce_norm_kernel, dim3(m), dim3(kThreads), 0, mg_stream(stream), 1, po, h, bias,
+                        n, norm, w, wb, eps, static_cast<__nv_bfloat16*>(x)));
+  return MG_OK;
+}

@@ -74,6 +74,41 @@ static inline cudaError_t mg_launch(void (*kernel)(KArgs...), dim3 grid, dim3 bl
 }
 
 // ---------------------------------------------------------------------------------------------
+// Peer-memory exchange of the row-parallel linears (tensor parallelism over NVLink / NVSwitch).
+// Every rank owns one device allocation, mapped into every other rank's process through CUDA IPC:
+//   recv  u64 [2 sets][world][slot]   rank r's partial of all-reduce e lands in set e%2, slot r
+// plus two local counters (all-reduces pushed by this rank; CTAs done in the push under way).
+// Each receive word carries its own flag: low half = the fp32 partial, high half = the epoch e
+// of the all-reduce that wrote it. An aligned 64-bit store is single-copy atomic, so a reader
+// that sees epoch e in a word also sees that word's value; no fence or separate flag is needed.
+// ---------------------------------------------------------------------------------------------
+#define MG_MAX_RANKS 8
+#define MG_EPI_PEER_F32 5  // internal epilogue: push acc*scale to every rank's receive slot
+
+struct PeerOut {
+  uint64_t* recv[MG_MAX_RANKS];    // each rank's receive area, as mapped in this process
+  uint32_t* count;                 // this rank: all-reduces pushed so far (= epoch of the last one)
+  uint32_t* done;                  // this rank: CTAs finished in the push under way
+  int64_t slot;                    // words per (set, rank) slot
+  int rank, world;
+};
+
+// Host: the PeerOut of a communicator made by mg_comm_create / mg_comm_open (comm.cu).
+int mg_comm_peer_out(void* comm, PeerOut* out);
+
+__device__ __forceinline__ void st_volatile_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_volatile_v2u64(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Small math helpers
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {

@@ -9,16 +9,19 @@
 //   M=128 dimension and the tokens its N (= MP, the token count padded to 16..256),
 //   so a decode batch of 1..256 tokens is one MMA tile per 128 weight rows.
 //   Per 128-wide K block:
-//     warp 4      TMA-loads the int8 weight tile [128 rows x 128 B] (128B-swizzled)
-//                 and the activation tile [MP x 128] bf16 (two 64-wide swizzled boxes);
-//     warps 0..3  (thread t <-> weight row t <-> TMEM lane t) convert the int8 row
-//                 to bf16 (exact) and tcgen05.st it into a TMEM A buffer;
-//     warp 5      issues 8 x tcgen05.mma kind::f16 (A from TMEM, B = activations
+//     warp 8      TMA-loads the int8 weight tile [128 rows x 128 B] (128B-swizzled) into
+//                 the weight ring and the activation tile [MP x 128] bf16 (two 64-wide
+//                 swizzled boxes) into the activation ring;
+//     warps 0..7  (warp w: TMEM lane quarter w%4, K half w/4; thread <-> weight row) pull
+//                 their bytes into registers (freeing the weight stage), convert them to
+//                 bf16 (exact) and tcgen05.st them into a TMEM A buffer;
+//     warp 9      issues 8 x tcgen05.mma kind::f16 (A from TMEM, B = activations
 //                 from shared memory) accumulating fp32 into TMEM.
 //   Split-K: the `split` CTAs of a thread-block cluster share one 128-row tile and
 //   divide its K blocks; after the mainloop each CTA parks its fp32 accumulator in
 //   shared memory and the cluster reduces it through distributed shared memory
-//   (fixed order, deterministic), applying scale, bias and the epilogue.
+//   (fixed order, deterministic), applying scale, bias and the epilogue — or, for a
+//   row-parallel linear, pushing the tile into every rank's receive slot (comm.cu).
 #include <mutex>
 
 #include "common.cuh"
@@ -190,7 +193,7 @@ template <int MP>
 __global__ void __launch_bounds__(kTcThreads, 1)
     i8_gemm_tc(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, int M, int K,
                int64_t N, const float* __restrict__ scales, const float* __restrict__ bias, void* y, int64_t ldy,
-               int epi, int split, int packed) {
+               int epi, int split, int packed, const PeerOut po) {
   using C = TcCfg<MP>;
   constexpr int SW = C::kWStages;
   constexpr int SX = C::kXStages;
@@ -393,6 +396,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t rbase[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) rbase[j] = (split > 1 && j < split) ? mapa_shared(red_addr, j) : red_addr;
+    // Row-parallel push: the partial of all-reduce e goes to slot [e%2][rank] of every rank, each
+    // word tagged with e. The previous push finished before this grid's dependency wait returned.
+    const bool peer = epi == MG_EPI_PEER_F32;
+    const uint32_t epoch = peer ? *reinterpret_cast<volatile uint32_t*>(po.count) + 1u : 0u;
+    const uint64_t tag = (uint64_t)epoch << 32;
     if (active) {
       for (int ml = (int)crank + half * split; ml < m_valid; ml += 2 * split) {
         const int m = m_base + ml;
@@ -413,7 +421,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           v0 += p0[j];
           v1 += p1[j];
         }
-        if (!swiglu) {
+        if (peer) {
+          const uint64_t word = tag | __float_as_uint(v0 * s0);
+          const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + (int64_t)m * N + n0;
+          for (int r = 0; r < po.world; ++r) st_volatile_u64(po.recv[r] + off, word);
+        } else if (!swiglu) {
           store_out(epi, y, (int64_t)m * ldy + n0, v0 * s0 + b0);
         } else {
           const float gv = v0 * s0 + b0, uv = v1 * s1 + b1;
@@ -427,6 +439,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
+  }
+  // The last CTA to finish advances this rank's all-reduce count, which the reduce kernel (the next
+  // grid) reads as the epoch to wait for. Every CTA read the count before counting itself.
+  if (epi == MG_EPI_PEER_F32 && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(po.done, 1u) == gridDim.x * gridDim.y - 1u) {
+      *reinterpret_cast<volatile uint32_t*>(po.done) = 0u;
+      *reinterpret_cast<volatile uint32_t*>(po.count) += 1u;
+    }
   }
 }
 
@@ -486,7 +507,7 @@ int auto_split(int64_t tiles, int kblocks, int ctas_per_sm) {
 template <int MP>
 int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
               const float* bias, int64_t n, void* y, int64_t ldy, int epi, int split, cudaStream_t st,
-              bool packed) {
+              bool packed, const PeerOut* po) {
   using C = TcCfg<MP>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -509,14 +530,14 @@ int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
   if (split > 8 || tiles * split > 0x7fffffff || mtiles > 65535) return MG_ERR_UNSUPPORTED;
   MG_CUDA_TRY(mg_launch(i8_gemm_tc<MP>, dim3((unsigned)(tiles * split), (unsigned)mtiles, 1), dim3(kTcThreads),
                         C::kSmemBytes, st, (unsigned)split, mw, mx, (int)m, (int)k, n, scales, bias, y, ldy, epi,
-                        split, packed ? 1 : 0));
+                        split, packed ? 1 : 0, po ? *po : PeerOut{}));
   return MG_OK;
 }
 
 int dispatch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
                 const float* bias, int64_t n, void* y, int64_t ldy, int epi, int split_k, cudaStream_t st,
-                bool packed) {
-#define MG_TC(MPV) launch_tc<MPV>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st, packed)
+                bool packed, const PeerOut* po = nullptr) {
+#define MG_TC(MPV) launch_tc<MPV>(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, split_k, st, packed, po)
   if (m <= 16) return MG_TC(16);
   if (m <= 32) return MG_TC(32);
   if (m <= 64) return MG_TC(64);
@@ -610,4 +631,18 @@ extern "C" int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t 
 extern "C" int mg_i8_linear(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
                             const float* bias, int64_t n, void* y, int64_t ldy, int epi, void* stream) {
   return mg_i8_linear_tc(x, m, k, ldx, q, scales, bias, n, y, ldy, epi, 0, stream);
+}
+
+extern "C" int mg_i8_linear_packed_rowpar(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                                          const float* scales, int64_t n, void* comm, int split_k, void* stream) {
+  PeerOut po;
+  int rc = mg_comm_peer_out(comm, &po);
+  if (rc) return rc;
+  if (m < 0 || k <= 0 || n <= 0 || !x || !packed || !scales || k % 16 || ldx < k || ldx % 8 || split_k < 0 ||
+      split_k > 8 || m * n > po.slot || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(packed)) & 15))
+    return MG_ERR_INVALID_ARG;
+  if (k > 0x7fffffff || m > 0x7fffffff) return MG_ERR_UNSUPPORTED;
+  if (m == 0) return MG_OK;
+  return dispatch_tc(x, m, k, ldx, packed, scales, nullptr, n, nullptr, n, MG_EPI_PEER_F32, split_k,
+                     mg_stream(stream), true, &po);
 }

@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import contextlib
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -194,10 +195,10 @@ class WeightLoader:
             layers.append(LayerWeights(
                 ln1_w=self.f32(ln1[0]), ln1_b=self.bias(ln1[1]),
                 qkv_q=torch.cat(parts_q).contiguous(), qkv_s=torch.cat(parts_s).contiguous(), qkv_b=qkv_b,
-                o_q=self.cols(o_q, qn), o_s=o_s, o_b=self.bias(bo) if self.rank == 0 else None,
+                o_q=self.cols(o_q, qn), o_s=o_s, o_b=self.bias(bo),
                 ln2_w=self.f32(ln2[0]), ln2_b=self.bias(ln2[1]),
                 gu_q=gu_q, gu_s=gu_s, gu_b=gu_b,
-                d_q=self.cols(d_q, s.inter), d_s=d_s, d_b=self.bias(bd) if self.rank == 0 else None))
+                d_q=self.cols(d_q, s.inter), d_s=d_s, d_b=self.bias(bd)))
         if gpt2:
             embed, wpe = self.f32(state["transformer.wte.weight"]), self.f32(state["transformer.wpe.weight"])
             norm_w, norm_b = self.f32(state["transformer.ln_f.weight"]), self.f32(state["transformer.ln_f.bias"])
@@ -264,6 +265,11 @@ class DecodeEngine:
         # pinned host staging for step inputs: tokens, positions, slots, ctx, then the table
         self.stage = torch.zeros(4 * B + B * max_blocks_per_seq, dtype=torch.int32, pin_memory=True)
         self.graphs: dict = {}
+        # TP > 1: row-parallel linears push their partials straight into every rank's memory and a
+        # fused reduce(+norm) kernel finishes the all-reduce (MG_FUSED_AR=0 falls back to NCCL).
+        self.comm = None
+        if world > 1 and os.environ.get("MG_FUSED_AR", "1") != "0" and isinstance(weights.lm_q, K.PackedWeight):
+            self.comm = K.Comm(rank, world, max_batch * spec.hidden, group=group)
 
     # ---- the step -----------------------------------------------------------------------------
     def _norm(self, h, w, b, x):
@@ -295,9 +301,16 @@ class DecodeEngine:
         attn_bytes = kv_tokens * self.hkv * D * 2 * 2 + b * self.hq * D * (4 + 2)
         with P("embed", b * H * 8):
             K.embed(self.tokens[:b], self.positions[:b], w.embed, w.wpe, h)
-        for l, L in enumerate(w.layers):
+        fused = self.comm is not None
+        norm_kind = K.NORM_LAYER if s.family == "gpt2" else K.NORM_RMS
+        push_bytes = b * H * 4 * self.world
+        if fused:  # later norms come out of the fused reduce of the preceding row-parallel linear
             with P("norm", b * H * 6):
-                self._norm(h, L.ln1_w, L.ln1_b, x)
+                self._norm(h, w.layers[0].ln1_w, w.layers[0].ln1_b, x)
+        for l, L in enumerate(w.layers):
+            if not fused:
+                with P("norm", b * H * 6):
+                    self._norm(h, L.ln1_w, L.ln1_b, x)
             with P("i8_linear", self.linear_bytes(L.qkv_q, b, 4, nqkv)):
                 K.i8_linear(x, L.qkv_q, L.qkv_s, L.qkv_b, y=self.qkv[:b], epilogue=K.EPI_STORE_F32)
             with P("rope_kv_append", b * nqkv * 4 + b * self.hq * D * 4 + b * 2 * self.hkv * D * 2):
@@ -306,20 +319,37 @@ class DecodeEngine:
             with P("paged_attn", attn_bytes):
                 K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
                                     n_shared_blocks=n_shared_blocks, out=self.attn[:b], workspace=self.workspace)
-            with P("i8_linear", self.linear_bytes(L.o_q, b, 8, H)):
-                row_parallel_residual(h, lambda y, e: K.i8_linear(self.attn[:b], L.o_q, L.o_s, L.o_b, y=y, epilogue=e),
-                                      self.rank, self.world, self.group)
-            with P("norm", b * H * 6):
-                self._norm(h, L.ln2_w, L.ln2_b, x)
+            if fused:
+                with P("i8_linear", self.linear_bytes(L.o_q, b, 0, H) + push_bytes):
+                    K.i8_linear_rowpar(self.attn[:b], L.o_q, L.o_s, self.comm)
+                with P("rowpar_reduce", push_bytes + b * H * 10):
+                    K.rowpar_reduce_norm(self.comm, h, L.o_b, norm_kind, L.ln2_w, L.ln2_b, s.eps, x)
+            else:
+                bias_o = L.o_b if self.rank == 0 else None
+                with P("i8_linear", self.linear_bytes(L.o_q, b, 8, H)):
+                    row_parallel_residual(h, lambda y, e: K.i8_linear(self.attn[:b], L.o_q, L.o_s, bias_o, y=y,
+                                                                      epilogue=e), self.rank, self.world, self.group)
+                with P("norm", b * H * 6):
+                    self._norm(h, L.ln2_w, L.ln2_b, x)
             epi_mlp = K.EPI_GELU_BF16 if s.family == "gpt2" else K.EPI_SWIGLU_BF16
             with P("i8_linear", self.linear_bytes(L.gu_q, b, 2, self.act.shape[1])):
                 K.i8_linear(x, L.gu_q, L.gu_s, L.gu_b, y=self.act[:b], epilogue=epi_mlp)
-            with P("i8_linear", self.linear_bytes(L.d_q, b, 8, H)):
-                row_parallel_residual(h, lambda y, e: K.i8_linear(self.act[:b], L.d_q, L.d_s, L.d_b, y=y, epilogue=e),
-                                      self.rank, self.world, self.group)
+            if fused:
+                nxt_w, nxt_b = ((w.layers[l + 1].ln1_w, w.layers[l + 1].ln1_b) if l + 1 < len(w.layers)
+                                else (w.norm_w, w.norm_b))
+                with P("i8_linear", self.linear_bytes(L.d_q, b, 0, H) + push_bytes):
+                    K.i8_linear_rowpar(self.act[:b], L.d_q, L.d_s, self.comm)
+                with P("rowpar_reduce", push_bytes + b * H * 10):
+                    K.rowpar_reduce_norm(self.comm, h, L.d_b, norm_kind, nxt_w, nxt_b, s.eps, x)
+            else:
+                bias_d = L.d_b if self.rank == 0 else None
+                with P("i8_linear", self.linear_bytes(L.d_q, b, 8, H)):
+                    row_parallel_residual(h, lambda y, e: K.i8_linear(self.act[:b], L.d_q, L.d_s, bias_d, y=y,
+                                                                      epilogue=e), self.rank, self.world, self.group)
         if compute_logits:
-            with P("norm", b * H * 6):
-                self._norm(h, w.norm_w, w.norm_b, x)
+            if not fused:
+                with P("norm", b * H * 6):
+                    self._norm(h, w.norm_w, w.norm_b, x)
             with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, s.vocab)):
                 K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32)
             with P("argmax", b * s.vocab * 4):
@@ -374,3 +404,12 @@ class DecodeEngine:
 
     def release_graphs(self) -> None:
         self.graphs.clear()
+
+    def close(self) -> None:
+        """Drop the captured graphs and the peer-memory communicator. With TP > 1, call it on every rank
+        after a barrier: peers write into this rank's receive area until their last step is done."""
+        self.graphs.clear()
+        if self.comm is not None:
+            torch.cuda.synchronize(self.device)
+            self.comm.close()
+            self.comm = None

@@ -216,3 +216,68 @@ def decode_advance(tokens, next_tokens, positions, ctx_lens, slots, block_tables
 
 def check_device() -> None:
     _lib.check_device(torch.cuda.current_stream().cuda_stream)
+
+
+# ---- fused row-parallel all-reduce over peer memory --------------------------------------------
+NORM_NONE, NORM_RMS, NORM_LAYER = 0, 1, 2
+
+
+class Comm:
+    """This rank's peer-memory communicator (receive area + flags, mapped into every rank).
+
+    ``exchange(my_handle: bytes) -> list[bytes]`` returns every rank's IPC handle in rank order; by
+    default it is an ``all_gather_object`` over ``group``."""
+
+    def __init__(self, rank: int, world: int, slot_elems: int, group=None, exchange=None) -> None:
+        lib = _lib.load()
+        nbytes = lib.mg_comm_handle_bytes()
+        self._h = C.c_void_p()
+        handle = C.create_string_buffer(nbytes)
+        _lib.call("mg_comm_create", rank, world, int(slot_elems), C.byref(self._h), C.cast(handle, C.c_void_p))
+        mine = handle.raw
+        if exchange is None:
+            import torch.distributed as dist
+            handles = [None] * world
+            dist.all_gather_object(handles, mine, group=group)
+        else:
+            handles = exchange(mine)
+        if len(handles) != world or any(len(h) != nbytes for h in handles):
+            raise ValueError("one IPC handle per rank is needed")
+        allh = C.create_string_buffer(b"".join(handles), nbytes * world)
+        _lib.call("mg_comm_open", self._h, C.cast(allh, C.c_void_p))
+        self.rank, self.world, self.slot = rank, world, slot_elems
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if not self._h:
+            raise RuntimeError("communicator is closed")
+        return self._h
+
+    def close(self) -> None:
+        if self._h:
+            _lib.call("mg_comm_destroy", self._h)
+            self._h = C.c_void_p()
+
+
+def i8_linear_rowpar(x, q: PackedWeight, scales, comm: Comm, split_k: int = 0) -> None:
+    """This rank's partial x · (q·s)ᵀ, pushed into every rank's receive slot (no bias)."""
+    _need(x, torch.bfloat16, "x", contiguous=False)
+    _need(scales, torch.float32, "scales")
+    if not isinstance(q, PackedWeight):
+        raise TypeError("the row-parallel push runs on tile-packed codes")
+    n, k = q.shape
+    if x.dim() != 2 or x.stride(1) != 1 or x.shape[1] != k:
+        raise ValueError("x must be [m, k] with unit inner stride")
+    _lib.call("mg_i8_linear_packed_rowpar", _ptr(x), x.shape[0], k, x.stride(0), _ptr(q.data), _ptr(scales), n,
+              comm.handle, int(split_k), _stream())
+
+
+def rowpar_reduce_norm(comm: Comm, h, bias, norm: int, w=None, b=None, eps: float = 1e-5, x=None):
+    """h += Σ_ranks partial + bias (rank order); with norm, x = bf16(norm(h)). Returns x."""
+    _need(h, torch.float32, "h")
+    m, n = h.shape
+    if norm and x is None:
+        x = torch.empty((m, n), dtype=torch.bfloat16, device=h.device)
+    _lib.call("mg_rowpar_reduce_norm", comm.handle, _ptr(h), _ptr(bias), m, n, int(norm), _ptr(w), _ptr(b),
+              float(eps), _ptr(x), _stream())
+    return x

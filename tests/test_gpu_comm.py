@@ -1,0 +1,85 @@
+"""Fused row-parallel all-reduce on one GPU (the multi-GPU path is tests/test_gpu_tp.py).
+
+* world 1: the row-parallel push + reduce(+norm) equals ``h + x·(q·s)ᵀ + bias`` and the RMSNorm /
+  LayerNorm of it, against the fp64 oracle;
+* a missing peer: a world-2 communicator whose second rank never pushes — the reduce kernel's
+  bounded wait gives up after about a second, records MG_ERR_TIMEOUT, and the host raises
+  TimeoutError; the context stays usable (a later world-1 reduce still works).
+"""
+
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import linear as olin
+from oracle.quant import quantize_rows_i8
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(m, k, n, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    q, s = quantize_rows_i8(w)
+    x = torch.from_numpy(rng.standard_normal((m, k), dtype=np.float32)).to(torch.bfloat16)
+    h0 = rng.standard_normal((m, n)).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32) * np.float32(0.1)
+    g = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    gb = (0.1 * rng.standard_normal(n)).astype(np.float32)
+    return x, q, s, h0, bias, g, gb
+
+
+def _close(got, want, rtol, atol):
+    err = np.abs(np.asarray(got, np.float64) - want)
+    assert not (err > atol + rtol * np.abs(want)).any(), f"max err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("norm", [0, 1, 2])
+def test_world1_push_reduce_norm(norm):
+    from microgen_b200 import kernels as K
+    m, k, n = 24, 1024, 768
+    x, q, s, h0, bias, g, gb = _case(m, k, n, seed=norm)
+    comm = K.Comm(0, 1, m * n, exchange=lambda mine: [mine])
+    try:
+        d = lambda a: torch.from_numpy(a).cuda()
+        h = d(h0.copy())
+        pw = K.pack_weights(d(q))
+        for rep in range(2):  # the second push uses the other receive set
+            h.copy_(d(h0))
+            K.i8_linear_rowpar(x.cuda(), pw, d(s), comm)
+            xo = K.rowpar_reduce_norm(comm, h, d(bias), norm, d(g), d(gb), 1e-5)
+            torch.cuda.synchronize()
+            want_h = h0 + olin.i8_linear(x.float().numpy(), q, s, bias)
+            _close(h.cpu().numpy(), want_h, 1e-4, 1e-4)
+            if norm == 1:
+                want_x = g * (want_h / np.sqrt((want_h ** 2).mean(-1, keepdims=True) + 1e-5))
+                _close(xo.float().cpu().numpy(), want_x, 2e-2, 1e-2)
+            elif norm == 2:
+                mu = want_h.mean(-1, keepdims=True)
+                want_x = (want_h - mu) / np.sqrt(((want_h - mu) ** 2).mean(-1, keepdims=True) + 1e-5) * g + gb
+                _close(xo.float().cpu().numpy(), want_x, 2e-2, 1e-2)
+        K.check_device()
+    finally:
+        comm.close()
+
+
+def test_missing_peer_times_out_and_context_survives():
+    from microgen_b200 import kernels as K
+    m, k, n = 4, 256, 256
+    x, q, s, h0, bias, g, gb = _case(m, k, n, seed=9)
+    d = lambda a: torch.from_numpy(a).cuda()
+    # rank 0 of a world of 2 whose rank-1 slot maps to itself: nothing ever pushes as rank 1
+    comm = K.Comm(0, 2, m * n, exchange=lambda mine: [mine, mine])
+    try:
+        h = d(h0.copy())
+        K.i8_linear_rowpar(x.cuda(), K.pack_weights(d(q)), d(s), comm)
+        t0 = time.time()
+        K.rowpar_reduce_norm(comm, h, d(bias), 1, d(g), None, 1e-5)
+        with pytest.raises(TimeoutError):
+            K.check_device()
+        assert 0.5 < time.time() - t0 < 30
+    finally:
+        comm.close()
+    test_world1_push_reduce_norm(1)  # the context is still healthy

@@ -1,5 +1,6 @@
 """Tensor parallelism across real GPUs (needs >= 2): TP=2 decode through B200TensorParallelBackend,
-one process per GPU over NCCL, against TP=1 on the same seeded model. TP=2 is teacher-forced with the
+one process per GPU, against TP=1 on the same seeded model, with the row-parallel reduction either fused
+(partials pushed into peer memory by the linear's epilogue, reduced by the next norm kernel) or over NCCL. TP=2 is teacher-forced with the
 TP=1 greedy stream: logits must agree within the bf16 tolerance at every step, and the argmax must agree
 wherever TP=1's top-1/top-2 margin exceeds that tolerance (TP sums the row-parallel partials in another
 order, so only near-ties may flip). Skipped when fewer than two GPUs are visible."""
@@ -43,8 +44,10 @@ def _prompts():
     return [shared + prompt_ids(SHAPE["vocab"], 9, seed=20 + i) for i in range(4)]
 
 
-def _worker(rank, world, port, outdir, graph, forced):
+def _worker(rank, world, port, outdir, graph, forced, fused):
     import torch.distributed as dist
+    os.environ["MG_FUSED_AR"] = "1" if fused else "0"
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     from microgen_b200.backends import B200TensorParallelBackend
     from tests._hf_models import make_hf_model
     torch.cuda.set_device(rank)
@@ -55,15 +58,20 @@ def _worker(rank, world, port, outdir, graph, forced):
                                    use_cuda_graph=graph, free_list_seed=1)
     be.load_model("tiny", model_instance=model)
     out = _decode(be, _prompts(), forced)
+    assert (be.engine.comm is not None) == fused
     be.engine.release_graphs()
     torch.save(out, os.path.join(outdir, f"r{rank}.pt"))
+    torch.cuda.synchronize()
+    dist.barrier()
+    be.engine.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("fused", [True, False], ids=["fused_push", "nccl"])
 @pytest.mark.parametrize("graph", [False, True])
-def test_tp2_matches_tp1(graph):
+def test_tp2_matches_tp1(graph, fused):
     import torch.multiprocessing as mp
     from microgen_b200.backends import B200QuantizedBackend
     from tests._hf_models import make_hf_model
@@ -72,7 +80,7 @@ def test_tp2_matches_tp1(graph):
     be.load_model("tiny", model_instance=model)
     ref_toks, ref_lg = _decode(be, _prompts())
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks, fused), nprocs=2, join=True)
         outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(2)]
     tol = 1e-2 + 2e-2 * np.abs(ref_lg)
     top2 = np.sort(ref_lg, axis=-1)[..., -2:]
