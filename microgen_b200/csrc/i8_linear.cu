@@ -33,6 +33,10 @@ __device__ __forceinline__ float gelu_tanh_f(float v) {
   return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
 }
 
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ void store_out(int epi, void* y, int64_t idx, float v) {
   switch (epi) {
     case MG_EPI_STORE_BF16: static_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v); break;
@@ -156,6 +160,7 @@ constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kTcThreads = 320;
 constexpr uint32_t kWStageBytes = kBN * kBK;  // int8 tile
+constexpr int kRedLoads = 16;                 // split-K partial loads in flight per thread
 
 template <int MP>
 struct TcCfg {
@@ -171,13 +176,84 @@ struct TcCfg {
   static constexpr uint32_t kRedBytes = MP * kBN * 4;
   static constexpr uint32_t kMainBytes = kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes;
   static constexpr uint32_t kBarOffset = kMainBytes;
-  static constexpr uint32_t kSmemBytes = kMainBytes + 256 + 1024;  // barriers + alignment slack
+  static constexpr uint32_t kSmemBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kAccCol = kABufs * 64;
   static constexpr uint32_t kTmemCols = (kAccCol + MP) <= 256 ? 256 : 512;
   // D=fp32 (bit 4), A=B=bf16 (bits 7, 10), K-major A and B, N = MP, M = 128.
   static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MP >> 3) << 17) |
                                      ((uint32_t)(kBN >> 4) << 24);
 };
+
+// Split-K reduction of one thread's columns ml0, ml0 + 2S, ... (< m_valid) at weight row r0: the
+// S partials of each column come from the `red` buffers of the S CTAs of the cluster (fixed CTA
+// order). Loads are issued in batches of about kRedLoads before any is consumed, so a batch costs
+// one distributed-shared-memory latency.
+template <int S, int MP, bool SWI, typename Emit>
+__device__ __forceinline__ void reduce_cols(uint32_t red_addr, int r0, int ml0, int m_valid, Emit& emit) {
+  constexpr int kCols = MP / (2 * S) > 0 ? MP / (2 * S) : 1;
+  constexpr int kPer = S * (SWI ? 2 : 1);
+  constexpr int kCB = kRedLoads / kPer > 0 ? (kRedLoads / kPer < kCols ? kRedLoads / kPer : kCols) : 1;
+  uint32_t base[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) base[j] = S > 1 ? mapa_shared(red_addr, (uint32_t)j) : red_addr;
+#pragma unroll 1
+  for (int c0 = 0; c0 < kCols; c0 += kCB) {
+    float p0[kCB][S], p1[kCB][SWI ? S : 1];
+#pragma unroll
+    for (int c = 0; c < kCB; ++c) {
+      const int ml = ml0 + (c0 + c) * 2 * S;
+      const bool ok = c0 + c < kCols && ml < m_valid;
+#pragma unroll
+      for (int j = 0; j < S; ++j) {
+        const uint32_t a = base[j] + (uint32_t)((ml * kBN + r0) * 4);
+        p0[c][j] = ok ? ld_dsmem_f32(a) : 0.f;
+        if (SWI) p1[c][j] = ok ? ld_dsmem_f32(a + 64 * 4) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kCB; ++c) {
+      const int ml = ml0 + (c0 + c) * 2 * S;
+      if (c0 + c < kCols && ml < m_valid) {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+          a0 += p0[c][j];
+          if (SWI) a1 += p1[c][j];
+        }
+        emit(ml, a0, a1);
+      }
+    }
+  }
+}
+
+// Any other split (an explicit split_k of 3, 5, 6 or 7): one column at a time.
+template <typename Emit>
+__device__ __forceinline__ void reduce_cols_any(uint32_t red_addr, int r0, int ml0, int m_valid, int split,
+                                                bool swiglu, Emit& emit) {
+  for (int ml = ml0; ml < m_valid; ml += 2 * split) {
+    const uint32_t off = (uint32_t)((ml * kBN + r0) * 4);
+    float p0[8], p1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      p0[j] = 0.f;
+      p1[j] = 0.f;
+      if (j < split) {
+        const uint32_t a = mapa_shared(red_addr, (uint32_t)j) + off;
+        p0[j] = ld_dsmem_f32(a);
+        if (swiglu) p1[j] = ld_dsmem_f32(a + 64 * 4);
+      }
+    }
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < split) {
+        a0 += p0[j];
+        a1 += p1[j];
+      }
+    }
+    emit(ml, a0, a1);
+  }
+}
 
 // Shared-memory descriptor of a K-major, 128B-swizzled bf16 tile (8-row x 128 B atoms, 1024 B apart).
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
@@ -190,7 +266,7 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
 }
 
 template <int MP>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
     i8_gemm_tc(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, int M, int K,
                int64_t N, const float* __restrict__ scales, const float* __restrict__ bias, void* y, int64_t ldy,
                int epi, int split, int packed, const PeerOut po) {
@@ -371,13 +447,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_before();
   }
   if (split > 1) cluster_sync_all(); else __syncthreads();
+  if (warp == kMmaWarp) {  // the accumulator is out of TMEM
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
 
   // ---------------- split-K reduction + epilogue ----------------
   // CTA `crank` owns token columns ml ≡ crank (mod split); within the CTA, converter thread t takes
   // weight row t % 128 and every second owned column (t / 128). For SwiGLU only rows < 64 are
-  // active, each reducing its gate/up pair (t, t+64). All `split` partials of an element are loaded
-  // before any is added (one distributed-shared-memory latency per element), and the sum runs in
-  // fixed CTA order (deterministic).
+  // active, each reducing its gate/up pair (t, t+64). A thread's (column, split) partials are read
+  // through distributed shared memory in batches (reduce_cols); each column sums its partials in
+  // fixed CTA order (deterministic). The residual add is a fire-and-forget reduction into y: exactly one thread
+  // adds to each element, so the result does not depend on timing.
   if (warp < kConvWarps) {
     const int t = threadIdx.x;
     const int half = t >> 7;
@@ -393,52 +474,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const float b0 = (active && bias) ? bias[n0] : 0.f;
     const float s1 = (active && swiglu) ? scales[n1] : 0.f;
     const float b1 = (active && swiglu && bias) ? bias[n1] : 0.f;
-    uint32_t rbase[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) rbase[j] = (split > 1 && j < split) ? mapa_shared(red_addr, j) : red_addr;
     // Row-parallel push: the partial of all-reduce e goes to slot [e%2][rank] of every rank, each
     // word tagged with e. The previous push finished before this grid's dependency wait returned.
     const bool peer = epi == MG_EPI_PEER_F32;
     const uint32_t epoch = peer ? *reinterpret_cast<volatile uint32_t*>(po.count) + 1u : 0u;
     const uint64_t tag = (uint64_t)epoch << 32;
-    if (active) {
-      for (int ml = (int)crank + half * split; ml < m_valid; ml += 2 * split) {
-        const int m = m_base + ml;
-        const uint32_t off0 = (uint32_t)((ml * kBN + r0) * 4);
-        float p0[8], p1[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          p0[j] = 0.f;
-          p1[j] = 0.f;
-          if (j < split) {
-            p0[j] = ld_dsmem_f32(rbase[j] + off0);
-            if (swiglu) p1[j] = ld_dsmem_f32(rbase[j] + off0 + 64 * 4);
-          }
-        }
-        float v0 = 0.f, v1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          v0 += p0[j];
-          v1 += p1[j];
-        }
-        if (peer) {
-          const uint64_t word = tag | __float_as_uint(v0 * s0);
-          const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + (int64_t)m * N + n0;
-          for (int r = 0; r < po.world; ++r) st_volatile_u64(po.recv[r] + off, word);
-        } else if (!swiglu) {
-          store_out(epi, y, (int64_t)m * ldy + n0, v0 * s0 + b0);
-        } else {
-          const float gv = v0 * s0 + b0, uv = v1 * s1 + b1;
-          static_cast<__nv_bfloat16*>(y)[(int64_t)m * ldy + (int64_t)tile * 64 + r0] =
-              __float2bfloat16_rn(silu_f(gv) * uv);
-        }
+    const int ml0 = (int)crank + half * split;
+    auto emit = [&](int ml, float a0, float a1) {
+      const int m = m_base + ml;
+      if (peer) {
+        const uint64_t word = tag | __float_as_uint(a0 * s0);
+        const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + (int64_t)m * N + n0;
+        for (int r = 0; r < po.world; ++r) st_volatile_u64(po.recv[r] + off, word);
+      } else if (epi == MG_EPI_ADD_F32) {
+        red_add_f32(static_cast<float*>(y) + (int64_t)m * ldy + n0, a0 * s0 + b0);
+      } else if (!swiglu) {
+        store_out(epi, y, (int64_t)m * ldy + n0, a0 * s0 + b0);
+      } else {
+        const float gv = a0 * s0 + b0, uv = a1 * s1 + b1;
+        static_cast<__nv_bfloat16*>(y)[(int64_t)m * ldy + (int64_t)tile * 64 + r0] =
+            __float2bfloat16_rn(silu_f(gv) * uv);
       }
+    };
+    if (active) {
+#define MG_RED(S)                                                                                      \
+  (swiglu ? reduce_cols<S, MP, true>(red_addr, r0, ml0, m_valid, emit)                                  \
+          : reduce_cols<S, MP, false>(red_addr, r0, ml0, m_valid, emit))
+      switch (split) {
+        case 1: MG_RED(1); break;
+        case 2: MG_RED(2); break;
+        case 4: MG_RED(4); break;
+        case 8: MG_RED(8); break;
+        default: reduce_cols_any(red_addr, r0, ml0, m_valid, split, swiglu, emit); break;
+      }
+#undef MG_RED
     }
   }
-  if (split > 1) cluster_sync_all(); else __syncthreads();
-  if (warp == kMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+  if (split > 1) {
+    cluster_sync_all();  // peers may still be reading this CTA's partials
+  } else if (epi == MG_EPI_PEER_F32) {
+    __syncthreads();     // every thread has read the count
   }
   // The last CTA to finish advances this rank's all-reduce count, which the reduce kernel (the next
   // grid) reads as the epoch to wait for. Every CTA read the count before counting itself.
@@ -495,13 +570,14 @@ int sm_count() {
   return n;
 }
 
+// Split-K factor: the largest power of two (cluster of 1, 2, 4 or 8 CTAs) with tiles x split within
+// one wave of resident CTAs and at least two K blocks per CTA. Power-of-two clusters pack the GPCs
+// without leftover SMs; a cluster that does not fit waits for a second wave.
 int auto_split(int64_t tiles, int kblocks, int ctas_per_sm) {
   const int64_t slots = (int64_t)sm_count() * ctas_per_sm;
-  int s = (int)(slots / (tiles > 0 ? tiles : 1));
-  s = s < 1 ? 1 : s;
-  s = s > 8 ? 8 : s;
-  const int max_by_k = kblocks / 2 > 0 ? kblocks / 2 : 1;
-  return s > max_by_k ? max_by_k : s;
+  int s = 1;
+  while (s < 8 && tiles * (s * 2) <= slots && kblocks >= 4 * s) s *= 2;
+  return s;
 }
 
 template <int MP>

@@ -95,7 +95,7 @@ def test_linear_store_bf16_vs_oracle(algo, m, k, n):
     close(y.float().cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("split", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 8])
 def test_linear_tc_split_k_deterministic_and_close(split):
     x, q, s, b = _mk_linear(32, 3072, 768, seed=4)
     y = K().i8_linear(dev(x, torch.bfloat16), dev(q), dev(s), dev(b), epilogue=K().EPI_STORE_F32, algo="tc",
@@ -105,6 +105,25 @@ def test_linear_tc_split_k_deterministic_and_close(split):
     y2 = K().i8_linear(dev(x, torch.bfloat16), dev(q), dev(s), dev(b), epilogue=K().EPI_STORE_F32, algo="tc",
                        split_k=split)
     assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("m,split", [(16, 8), (9, 4), (32, 2), (20, 8), (32, 1), (64, 4)])
+def test_linear_tc_split_reduction_epilogues(m, split):
+    """Split-K reductions (power-of-two splits run the batched reduction, others the per-column one)
+    with the residual-add and SwiGLU epilogues."""
+    k_ = K()
+    k, n = 2048, 256
+    x, q, s, b = _mk_linear(m, k, n, seed=m * 10 + split)
+    want = olin.i8_linear(x, q, s, b)
+    xd, qd, sd, bd = dev(x, torch.bfloat16), dev(q), dev(s), dev(b)
+    base = np.random.default_rng(split).standard_normal((m, n)).astype(np.float32)
+    acc = dev(base)
+    k_.i8_linear(xd, qd, sd, bd, y=acc, epilogue=k_.EPI_ADD_F32, algo="tc", split_k=split)
+    close(acc.cpu().numpy(), base + want, rtol=1e-4, atol=1e-4)
+    sw = k_.i8_linear(xd, qd, sd, bd, epilogue=k_.EPI_SWIGLU_BF16, algo="tc", split_k=split)
+    wr = want.reshape(m, n // 128, 2, 64)
+    gate, up = wr[:, :, 0, :].reshape(m, -1), wr[:, :, 1, :].reshape(m, -1)
+    close(sw.float().cpu().numpy(), gate / (1 + np.exp(-gate)) * up)
 
 
 @pytest.mark.parametrize("algo", ["simt", "tc"])
