@@ -1,5 +1,6 @@
-// C-ABI plumbing: status strings, error words, version.
+// C-ABI plumbing: status strings, error words, version, TMA descriptors.
 #include <cstdlib>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -19,6 +20,36 @@ bool mg_pdl_enabled() {
 int mg_set_cuda_error(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);
   return MG_ERR_CUDA;
+}
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled_t get_encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+  });
+  return fn;
+}
+
+int mg_make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  PFN_encodeTiled_t enc = get_encode_fn();
+  if (!enc) return MG_ERR_CUDA;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MG_OK : MG_ERR_INVALID_ARG;
 }
 
 extern "C" int mg_abi_version(void) { return MG_ABI_VERSION; }

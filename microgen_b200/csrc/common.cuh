@@ -46,6 +46,10 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 
 bool mg_pdl_enabled();
 
+// Host: a 2-D tiled TMA descriptor (row-major [outer][inner], row_bytes apart; box_inner x box_outer).
+int mg_make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+
 template <typename... KArgs, typename... Args>
 static inline cudaError_t mg_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                                     unsigned cluster, Args&&... args) {

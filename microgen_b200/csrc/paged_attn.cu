@@ -1,49 +1,57 @@
 // Paged-KV decode attention (one query token per sequence) over 16-token blocks.
 //
 // Pools are bf16 [num_blocks, hkv, 16, d]: one (block, kv head) tile is 16*d contiguous
-// elements. The query heads of one GQA group (hq/hkv <= 16) form the 16 rows of an
-// m16n8k16 tile, so QKᵀ and PV run on the tensor cores and the kernel stays bound by
-// the KV bytes it streams.
+// elements, i.e. 16 rows of a 2-D tensor [num_blocks*hkv*16, d] that TMA reads. The query
+// heads of one GQA group (hq/hkv <= 16) form the 16 rows of an m16n8k16 tile, so QKᵀ and PV
+// run on the tensor cores and the kernel stays bound by the KV bytes it streams.
 //
+// A CTA is one producer warp (TMA loads of (K, V) tiles into a ring of kStages shared-memory
+// stages, 128-byte swizzled so the ldmatrix reads are conflict-free) and kCons consumer warps.
 // One launch covers two kinds of CTAs:
-//   * shared CTAs — one per (kv head, chunk of up to kChunk shared-prefix blocks). The
-//     chunk is loaded once into shared memory and every sequence's query group is run
-//     against it (rows = batch x group), so a prefix shared by the whole batch is read
-//     from HBM once per batch instead of once per sequence.
-//   * private CTAs — one per (sequence, kv head, split) over the sequence's own blocks.
-//     Four warps take interleaved blocks, each with its own double-buffered tiles and
+//   * shared CTAs — one per (kv head, chunk of up to kChunk shared-prefix blocks, group of
+//     kCons query row tiles). The chunk is loaded once and every sequence's query group is run
+//     against it (rows = batch x group), so a prefix shared by the whole batch is read from HBM
+//     once per batch instead of once per sequence.
+//   * private CTAs — one per (sequence, kv head, split) over the sequence's own blocks. Tile i
+//     of the split goes to stage i % kStages and consumer warp i % kCons (each warp owns
+//     kStages/kCons stages, so that many of its tiles are in flight); each warp keeps its own
 //     online-softmax state, merged at the end.
-// Each CTA leaves (m, l, unnormalised O) per query head in a workspace slot, and a
-// combine kernel merges the slots (log-sum-exp). With no shared prefix and one split
-// the private CTA writes the normalised output itself.
+// Each CTA leaves (m, l, unnormalised O) per query head in a workspace slot, and a combine
+// kernel merges the slots (log-sum-exp). With no shared prefix and one split the private CTA
+// writes the normalised output itself.
 #include "common.cuh"
 
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = 8;  // shared-prefix blocks per shared CTA
+constexpr int kCons = 4;                 // consumer warps
+constexpr int kProd = kCons;             // producer warp index
+constexpr int kThreads = (kCons + 1) * 32;
+constexpr int kStages = 8;               // KV ring stages (a multiple of kCons)
+constexpr int kChunk = 8;                // shared-prefix blocks per shared CTA (<= kStages)
+static_assert(kStages % kCons == 0 && kChunk <= kStages, "ring layout");
 
 template <int D>
 struct AttnCfg {
-  static constexpr int kStride = D + 8;                 // padded smem row (bf16): conflict-free ldmatrix
-  static constexpr int kTile = 16 * kStride;            // elements of one 16-token tile
-  static constexpr int kPrivBytes = kWarps * 2 * 2 * kTile * 2;  // per warp: 2 stages x (K,V)
-  static constexpr int kSharedBytes = kChunk * 2 * kTile * 2;
-  static constexpr int kMergeBytes = kWarps * 16 * (D + 2) * 4;
-  static constexpr int kSmem = (kPrivBytes > kSharedBytes ? kPrivBytes : kSharedBytes) > kMergeBytes
-                                   ? (kPrivBytes > kSharedBytes ? kPrivBytes : kSharedBytes)
-                                   : kMergeBytes;
+  static constexpr int kTileBytes = 16 * D * 2;          // K (or V) of one block and kv head
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kMergeBytes = kCons * 16 * (D + 2) * 4;
+  static constexpr int kMain = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
+  static constexpr int kBarOffset = (kMain + 7) / 8 * 8;
+  static constexpr int kSmem = kBarOffset + (2 * kStages + 1) * 8 + 1024;  // + 1 KB alignment slack
+  static constexpr int kBoxCols = D >= 64 ? 64 : D;       // one TMA box row = 128 B (64 B for d = 32)
 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Byte offset of (row, col) in a tile. d >= 64: halves of 64 columns, each 16 rows x 128 B with the
+// 16-byte chunks XOR-swizzled by row % 8 (TMA SWIZZLE_128B); d = 32: plain 64-byte rows.
+template <int D>
+__device__ __forceinline__ uint32_t swz(int row, int col) {
+  if constexpr (D >= 64) {
+    const int half = col >> 6, c = col & 63;
+    return (uint32_t)(half * 2048 + row * 128 + ((((c >> 3) ^ (row & 7))) << 4) + (c & 7) * 2);
+  } else {
+    return (uint32_t)(row * D * 2 + col * 2);
+  }
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -63,28 +71,39 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
-// Issue the async copies of one 16-token (K, V) tile of kv head h into smem rows of stride kStride.
-// Rows >= valid are zero-filled (never read from global).
+// TMA loads of the K and V tiles of (block phys, kv head h) into one ring stage.
 template <int D>
-__device__ __forceinline__ void load_tile(uint32_t ks, uint32_t vs, const __nv_bfloat16* kp, const __nv_bfloat16* vp,
-                                          int64_t blk, int hkv, int h, int valid, int lane, int nthreads) {
-  constexpr int kChunksPerRow = D / 8;  // 16-byte chunks
-  const int64_t base = ((blk * hkv + h) * 16) * (int64_t)D;
-  for (int c = lane; c < 16 * kChunksPerRow; c += nthreads) {
-    const int row = c / kChunksPerRow, col = (c % kChunksPerRow) * 8;
-    const bool ok = row < valid;
-    const uint32_t off = (uint32_t)(row * AttnCfg<D>::kStride + col) * 2;
-    cp_async16(ks + off, kp + base + row * D + col, ok);
-    cp_async16(vs + off, vp + base + row * D + col, ok);
+__device__ __forceinline__ void load_stage(uint8_t* st, const CUtensorMap* tk, const CUtensorMap* tv, uint64_t* bar,
+                                           int row) {
+  constexpr int T = AttnCfg<D>::kTileBytes;
+  mbar_arrive_expect_tx(bar, AttnCfg<D>::kStageBytes);
+#pragma unroll
+  for (int c = 0; c < D; c += AttnCfg<D>::kBoxCols) {
+    tma_load_2d(st + c * 32, tk, bar, c, row);  // 16 rows x 128 B = 2 KB per 64 columns
+    tma_load_2d(st + T + c * 32, tv, bar, c, row);
   }
+}
+
+// Zero V rows [valid, 16) of a stage (a partial last block: those pool slots hold no token, and
+// P = 0 there must not meet a NaN). The stage then goes back to the async proxy.
+template <int D>
+__device__ __forceinline__ void zero_v_tail(uint32_t vs, int valid, int lane) {
+  constexpr int kChunksPerRow = D / 8;
+  for (int c = valid * kChunksPerRow + lane; c < 16 * kChunksPerRow; c += 32) {
+    const int row = c / kChunksPerRow, col = (c % kChunksPerRow) * 8;
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vs + swz<D>(row, col)), "r"(0u) : "memory");
+  }
+  __syncwarp();
 }
 
 // Online-softmax update of one 16-row query tile with one 16-token KV tile.
 template <int D>
 __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uint32_t ks, uint32_t vs, int valid,
                                             float (&o)[D / 8][4], float (&m)[2], float (&l)[2], int lane) {
-  constexpr int kS = AttnCfg<D>::kStride;
   float s[2][4];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -95,7 +114,7 @@ __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uin
   for (int kk = 0; kk < D / 16; ++kk) {
     uint32_t b0, b1, b2, b3;
     const int tok = (j8 >> 1) * 8 + r8, d = kk * 16 + (j8 & 1) * 8;
-    ldsm_x4(ks + (uint32_t)(tok * kS + d) * 2, b0, b1, b2, b3);
+    ldsm_x4(ks + swz<D>(tok, d), b0, b1, b2, b3);
     mma_bf16(s[0], qa[kk], b0, b1);
     mma_bf16(s[1], qa[kk], b2, b3);
   }
@@ -141,9 +160,83 @@ __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uin
   for (int d2 = 0; d2 < D / 16; ++d2) {
     uint32_t b0, b1, b2, b3;
     const int tok = (j8 & 1) * 8 + r8, d = d2 * 16 + (j8 >> 1) * 8;
-    ldsm_x4_t(vs + (uint32_t)(tok * kS + d) * 2, b0, b1, b2, b3);
+    ldsm_x4_t(vs + swz<D>(tok, d), b0, b1, b2, b3);
     mma_bf16(o[2 * d2], pa, b0, b1);
     mma_bf16(o[2 * d2 + 1], pa, b2, b3);
+  }
+}
+
+// Transposed form for a private CTA (one sequence, group <= 8 query heads): Sᵀ = K Qᵀ with the 16
+// tokens of a block as the MMA rows and the (padded) heads as its 8 columns, then Oᵀ += Vᵀ Pᵀ with
+// 16 head dims per MMA row block: D/8 MMAs per block instead of D/4 when the MMA rows held the heads.
+// qb: B fragments of Qᵀ (k = dims, n = heads); o: Oᵀ accumulators (rows = dims, cols = heads);
+// m, l: running max / sum of heads 2t and 2t+1 (t = lane % 4).
+template <int D>
+__device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], uint32_t ks, uint32_t vs, int valid,
+                                              float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  const int arow = lane & 15, acol = (lane >> 4) * 8;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t a[4];
+    ldsm_x4(ks + swz<D>(arow, kk * 16 + acol), a[0], a[1], a[2], a[3]);
+    mma_bf16(s, a, qb[kk][0], qb[kk][1]);
+  }
+  if (g >= valid) s[0] = s[1] = -INFINITY;
+  if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float mx = fmaxf(s[r], s[2 + r]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mn = fmaxf(m[r], mx);
+    const float alpha = exp2f(m[r] - mn);
+    s[r] = exp2f(s[r] - mn);
+    s[2 + r] = exp2f(s[2 + r] - mn);
+    float sum = s[r] + s[2 + r];
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+    l[r] = l[r] * alpha + sum;
+    m[r] = mn;
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) {
+      o[dt][r] *= alpha;
+      o[dt][2 + r] *= alpha;
+    }
+  }
+  // Pᵀ as the B operand (k = tokens, n = heads): thread (g, t) needs tokens 2t, 2t+1, 2t+8, 2t+9 of
+  // head g, held (as halves of packed head pairs) by the threads of rows 2t and 2t+1.
+  const uint32_t lo = pack_bf16x2(s[0], s[1]), hi = pack_bf16x2(s[2], s[3]);
+  const int src = 8 * t + (g >> 1);
+  const uint32_t x = __shfl_sync(0xffffffffu, lo, src), y = __shfl_sync(0xffffffffu, lo, src + 4);
+  const uint32_t z = __shfl_sync(0xffffffffu, hi, src), w = __shfl_sync(0xffffffffu, hi, src + 4);
+  const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
+  const uint32_t b0 = __byte_perm(x, y, sel), b1 = __byte_perm(z, w, sel);
+  const int vtok = (lane & 7) + ((lane >> 4) << 3), vdim = ((lane >> 3) & 1) * 8;
+#pragma unroll
+  for (int dt = 0; dt < D / 16; ++dt) {
+    uint32_t a[4];
+    ldsm_x4_t(vs + swz<D>(vtok, dt * 16 + vdim), a[0], a[1], a[2], a[3]);
+    mma_bf16(o[dt], a, b0, b1);
+  }
+}
+
+// B fragments of Qᵀ for the transposed form: column n = head g (< group, else zero) of the sequence.
+template <int D>
+__device__ __forceinline__ void load_qt(uint32_t (&qb)[D / 16][2], const float* qh0, int group, float qscale,
+                                        int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const float* qh = g < group ? qh0 + g * D : nullptr;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int d0 = kk * 16 + 2 * t;
+    const float2 a = qh ? *reinterpret_cast<const float2*>(qh + d0) : make_float2(0.f, 0.f);
+    const float2 b = qh ? *reinterpret_cast<const float2*>(qh + d0 + 8) : make_float2(0.f, 0.f);
+    qb[kk][0] = pack_bf16x2(a.x * qscale, a.y * qscale);
+    qb[kk][1] = pack_bf16x2(b.x * qscale, b.y * qscale);
   }
 }
 
@@ -171,8 +264,6 @@ __device__ __forceinline__ void load_q(uint32_t (&qa)[D / 16][4], const float* q
 
 struct AttnParams {
   const float* q;
-  const __nv_bfloat16* kp;
-  const __nv_bfloat16* vp;
   int64_t num_blocks;
   const int32_t* tables;
   int max_blocks;
@@ -180,6 +271,7 @@ struct AttnParams {
   int b, hq, hkv, group;
   int n_shared;   // shared-prefix blocks
   int n_shared_ctas_per_head;
+  int n_row_groups;  // shared CTAs per (kv head, chunk): groups of kCons query row tiles
   int nsplit, bps;  // private splits and blocks per split
   int nslots;       // workspace slots per (seq, head) = shared chunks + nsplit
   float qscale;
@@ -189,83 +281,115 @@ struct AttnParams {
   bool direct;  // private CTA writes the final output
 };
 
-template <int D>
-__device__ void private_cta(const AttnParams& p, int pair, int sp, uint8_t* smem) {
+template <int D, bool T>
+__device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, int pair, int sp,
+                            uint8_t* smem, uint64_t* full, uint64_t* empty) {
   using C = AttnCfg<D>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = pair / p.hkv, h = pair % p.hkv;
+  const int b0 = p.n_shared + sp * p.bps;
+  const int32_t* table = p.tables + (int64_t)seq * p.max_blocks;
   const int ctx = p.ctx[seq];
   const int nblk = (ctx + 15) >> 4;
-  const int b0 = p.n_shared + sp * p.bps;
-  const int b1 = min(nblk, b0 + p.bps);
-  const int32_t* table = p.tables + (int64_t)seq * p.max_blocks;
-  if (ctx < 1 || nblk > p.max_blocks) {
-    if (threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 400);
-  }
-
-  uint32_t qa[D / 16][4];
-  const int g0 = lane >> 2, g1 = g0 + 8;
-  load_q<D>(qa, p.q, p.hq, g0 < p.group ? seq : -1, h * p.group + g0, g1 < p.group ? seq : -1, h * p.group + g1,
-            p.qscale, lane);
-  float o[D / 8][4];
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-
-  const uint32_t wbase = smem_u32(smem) + (uint32_t)(warp * 2 * 2 * C::kTile * 2);
-  auto kst = [&](int st) { return wbase + (uint32_t)(st * 2 * C::kTile * 2); };
-  auto vst = [&](int st) { return kst(st) + (uint32_t)(C::kTile * 2); };
-  auto fetch = [&](int j, int st) {
-    int64_t phys = table[j];
-    const int valid = min(16, ctx - j * 16);
-    if (phys < 0 || phys >= p.num_blocks) {
-      mg_record_error(MG_ERR_DEVICE, 401);
-      phys = 0;
-    }
-    load_tile<D>(kst(st), vst(st), p.kp, p.vp, phys, p.hkv, h, valid, lane, 32);
-  };
   const bool tables_ok = ctx >= 1 && nblk <= p.max_blocks;
-  int j = b0 + warp;
-  if (tables_ok && j < b1) fetch(j, 0);
-  cp_async_commit();
-  int st = 0;
-  for (; tables_ok && j < b1; j += kWarps) {
-    const int jn = j + kWarps;
-    if (jn < b1) fetch(jn, st ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncwarp();
-    attend_tile<D>(qa, kst(st), vst(st), min(16, ctx - j * 16), o, m, l, lane);
-    __syncwarp();
-    st ^= 1;
-  }
-  cp_async_wait<0>();
-  __syncthreads();
+  if (!tables_ok && threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 400);
+  const int ntiles = tables_ok ? max(0, min(nblk, b0 + p.bps) - b0) : 0;
+  const int g0 = lane >> 2, g1 = g0 + 8;
+  constexpr int kO = T ? D / 16 : D / 8;  // accumulator fragments: Oᵀ (T) or O
+  float o[kO][4];
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < kO; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-  // merge the four warps' states through shared memory: [warp][row][D + 2]
+  if (warp == kProd) {
+    // Block-table entries 32 at a time, one per lane, the next window loaded a window ahead.
+    auto entry = [&](int i) { return i < ntiles ? table[b0 + i] : 0; };
+    int cur = entry(lane), nxt = entry(32 + lane);
+    bool ok = true;
+    for (int i = 0; i < ntiles && ok; ++i) {
+      if (i > 0 && (i & 31) == 0) {
+        cur = nxt;
+        nxt = entry(i + 32 + lane);
+      }
+      int64_t phys = __shfl_sync(0xffffffffu, cur, i & 31);
+      if (phys < 0 || phys >= p.num_blocks) {
+        if (lane == 0) mg_record_error(MG_ERR_DEVICE, 401);
+        phys = 0;
+      }
+      if (lane == 0) {
+        const int s = i % kStages;
+        if (i >= kStages) ok = mbar_wait(&empty[s], ((i / kStages) - 1) & 1, 411);
+        if (ok) load_stage<D>(smem + s * C::kStageBytes, tk, tv, &full[s], (int)((phys * p.hkv + h) * 16));
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+  } else {
+    uint32_t qa[D / 16][T ? 2 : 4];
+    if constexpr (T) {
+      load_qt<D>(qa, p.q + ((int64_t)seq * p.hq + h * p.group) * D, p.group, p.qscale, lane);
+    } else {
+      load_q<D>(qa, p.q, p.hq, g0 < p.group ? seq : -1, h * p.group + g0, g1 < p.group ? seq : -1,
+                h * p.group + g1, p.qscale, lane);
+    }
+    for (int i = warp; i < ntiles; i += kCons) {
+      const int s = i % kStages;
+      if (!mbar_wait(&full[s], (i / kStages) & 1, 410)) break;
+      const uint32_t ks = smem_u32(smem + s * C::kStageBytes), vs = ks + C::kTileBytes;
+      const int valid = min(16, ctx - (b0 + i) * 16);
+      if (valid < 16) zero_v_tail<D>(vs, valid, lane);
+      if constexpr (T) {
+        attend_tile_t<D>(qa, ks, vs, valid, o, m, l, lane);
+      } else {
+        attend_tile<D>(qa, ks, vs, valid, o, m, l, lane);
+      }
+      if (valid < 16) fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  __syncthreads();  // every tile consumed: the ring is free for the merge
+
+  // merge the consumer warps' states through shared memory: [warp][row][D + 2]
   float* mg = reinterpret_cast<float*>(smem);
   const int c = (lane & 3) * 2;
+  if (T && warp < kCons) {
+    // Oᵀ fragment (dims dt*16 + g0 (+8), heads c, c+1) -> rows = heads
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = g0 + r * 8;
-    float* dst = mg + (warp * 16 + row) * (D + 2);
+    for (int r = 0; r < 2; ++r) {
+      float* dst = mg + (warp * 16 + c + r) * (D + 2);
 #pragma unroll
-    for (int dn = 0; dn < D / 8; ++dn) {
-      dst[dn * 8 + c] = o[dn][2 * r];
-      dst[dn * 8 + c + 1] = o[dn][2 * r + 1];
+      for (int dt = 0; dt < kO; ++dt) {
+        dst[dt * 16 + g0] = o[dt][r];
+        dst[dt * 16 + g0 + 8] = o[dt][2 + r];
+      }
+      if (g0 == 0) {
+        dst[D] = m[r];
+        dst[D + 1] = l[r];
+      }
     }
-    if ((lane & 3) == 0) {
-      dst[D] = m[r];
-      dst[D + 1] = l[r];
+  } else if (warp < kCons) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = g0 + r * 8;
+      float* dst = mg + (warp * 16 + row) * (D + 2);
+#pragma unroll
+      for (int dn = 0; dn < D / 8; ++dn) {
+        dst[dn * 8 + c] = o[dn][2 * r];
+        dst[dn * 8 + c + 1] = o[dn][2 * r + 1];
+      }
+      if ((lane & 3) == 0) {
+        dst[D] = m[r];
+        dst[D + 1] = l[r];
+      }
     }
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < p.group * D; idx += kThreads) {
     const int row = idx / D, d = idx % D;
     float M = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mg[(w * 16 + row) * (D + 2) + D]);
+    for (int w = 0; w < kCons; ++w) M = fmaxf(M, mg[(w * 16 + row) * (D + 2) + D]);
     float L = 0.f, O = 0.f;
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < kCons; ++w) {
       const float* src = mg + (w * 16 + row) * (D + 2);
       const float wgt = M == -INFINITY ? 0.f : exp2f(src[D] - M);
       L += src[D + 1] * wgt;
@@ -287,72 +411,91 @@ __device__ void private_cta(const AttnParams& p, int pair, int sp, uint8_t* smem
 }
 
 template <int D>
-__device__ void shared_cta(const AttnParams& p, int h, int chunk, uint8_t* smem) {
+__device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, int h, int chunk,
+                           int rg, uint8_t* smem, uint64_t* full) {
   using C = AttnCfg<D>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk0 = chunk * kChunk;
   const int nb = min(kChunk, p.n_shared - blk0);
-  const uint32_t base = smem_u32(smem);
   // shared blocks are the first n_shared entries of every table; read them from sequence 0's table
-  for (int i = 0; i < nb; ++i) {
-    int64_t phys = p.tables[blk0 + i];
+  if (warp == kProd) {
+    int64_t phys = lane < nb ? p.tables[blk0 + lane] : 0;
     if (phys < 0 || phys >= p.num_blocks) {
-      if (threadIdx.x == 0) mg_record_error(MG_ERR_DEVICE, 402);
+      mg_record_error(MG_ERR_DEVICE, 402);
       phys = 0;
     }
-    const uint32_t ks = base + (uint32_t)(i * 2 * C::kTile * 2);
-    load_tile<D>(ks, ks + C::kTile * 2, p.kp, p.vp, phys, p.hkv, h, 16, threadIdx.x, kThreads);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
-  const int rows = p.b * p.group;
-  const int ntiles = (rows + 15) / 16;
-  const int c = (lane & 3) * 2;
-  for (int t = warp; t < ntiles; t += kWarps) {
-    const int r0 = t * 16 + (lane >> 2), r1 = r0 + 8;
-    const int s0 = r0 < rows ? r0 / p.group : -1, s1 = r1 < rows ? r1 / p.group : -1;
-    uint32_t qa[D / 16][4];
-    load_q<D>(qa, p.q, p.hq, s0, h * p.group + (r0 % p.group), s1, h * p.group + (r1 % p.group), p.qscale, lane);
-    float o[D / 8][4];
-#pragma unroll
-    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     for (int i = 0; i < nb; ++i) {
-      const uint32_t ks = base + (uint32_t)(i * 2 * C::kTile * 2);
-      attend_tile<D>(qa, ks, ks + C::kTile * 2, 16, o, m, l, lane);
+      const int64_t ph = __shfl_sync(0xffffffffu, phys, i);
+      if (lane == 0) load_stage<D>(smem + i * C::kStageBytes, tk, tv, &full[i], (int)((ph * p.hkv + h) * 16));
     }
+    return;
+  }
+  const int rows = p.b * p.group;
+  const int t = rg * kCons + warp;  // this warp's 16-row query tile
+  if (t * 16 >= rows) return;
+  const int c = (lane & 3) * 2;
+  const int r0 = t * 16 + (lane >> 2), r1 = r0 + 8;
+  const int s0 = r0 < rows ? r0 / p.group : -1, s1 = r1 < rows ? r1 / p.group : -1;
+  uint32_t qa[D / 16][4];
+  load_q<D>(qa, p.q, p.hq, s0, h * p.group + (r0 % p.group), s1, h * p.group + (r1 % p.group), p.qscale, lane);
+  float o[D / 8][4];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int row = r ? r1 : r0;
-      if (row >= rows) continue;
-      const int seq = row / p.group, head = h * p.group + row % p.group;
-      const int64_t slot = ((int64_t)seq * p.hq + head) * p.nslots + chunk;
-      float* dst = p.ws_o + slot * D;
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  for (int i = 0; i < nb; ++i) {
+    if (!mbar_wait(&full[i], 0, 412)) return;
+    const uint32_t ks = smem_u32(smem + i * C::kStageBytes);
+    attend_tile<D>(qa, ks, ks + C::kTileBytes, 16, o, m, l, lane);
+  }
 #pragma unroll
-      for (int dn = 0; dn < D / 8; ++dn) {
-        dst[dn * 8 + c] = o[dn][2 * r];
-        dst[dn * 8 + c + 1] = o[dn][2 * r + 1];
-      }
-      if ((lane & 3) == 0) {
-        p.ws_ml[slot * 2] = m[r];
-        p.ws_ml[slot * 2 + 1] = l[r];
-      }
+  for (int r = 0; r < 2; ++r) {
+    const int row = r ? r1 : r0;
+    if (row >= rows) continue;
+    const int seq = row / p.group, head = h * p.group + row % p.group;
+    const int64_t slot = ((int64_t)seq * p.hq + head) * p.nslots + chunk;
+    float* dst = p.ws_o + slot * D;
+#pragma unroll
+    for (int dn = 0; dn < D / 8; ++dn) {
+      dst[dn * 8 + c] = o[dn][2 * r];
+      dst[dn * 8 + c + 1] = o[dn][2 * r + 1];
+    }
+    if ((lane & 3) == 0) {
+      p.ws_ml[slot * 2] = m[r];
+      p.ws_ml[slot * 2 + 1] = l[r];
     }
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads) paged_attn_kernel(const AttnParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
+template <int D, bool T>
+__global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(const __grid_constant__ CUtensorMap tk,
+                                                              const __grid_constant__ CUtensorMap tv,
+                                                              const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnCfg<D>::kBarOffset);
+  uint64_t* empty = full + kStages;
   griddep_launch();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  if (threadIdx.x == kProd * 32) {
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  __syncthreads();
   griddep_wait();
-  const int n_shared_ctas = p.n_shared_ctas_per_head * p.hkv;
+  const int n_shared_ctas = p.n_shared_ctas_per_head * p.n_row_groups * p.hkv;
   if ((int)blockIdx.x < n_shared_ctas) {
-    shared_cta<D>(p, blockIdx.x / p.n_shared_ctas_per_head, blockIdx.x % p.n_shared_ctas_per_head, smem);
+    const int per_head = p.n_shared_ctas_per_head * p.n_row_groups;
+    const int h = blockIdx.x / per_head, r = blockIdx.x % per_head;
+    shared_cta<D>(p, &tk, &tv, h, r / p.n_row_groups, r % p.n_row_groups, smem, full);
   } else {
     const int i = blockIdx.x - n_shared_ctas;
-    private_cta<D>(p, i / p.nsplit, i % p.nsplit, smem);
+    private_cta<D, T>(p, &tk, &tv, i / p.nsplit, i % p.nsplit, smem, full, empty);
   }
 }
 
@@ -376,7 +519,7 @@ __global__ void combine_kernel(const float* __restrict__ ws_o, const float* __re
 }
 
 struct Plan {
-  int n_shared_ctas_per_head, nsplit, bps, nslots;
+  int n_shared_ctas_per_head, n_row_groups, nsplit, bps, nslots;
   bool direct;
   size_t ws_bytes;
 };
@@ -392,14 +535,18 @@ int sm_count_attn() {
   return n;
 }
 
+// Splits: private CTAs for about two and a half waves of three CTAs per SM beside the shared CTAs
+// (small enough that the last wave's tail is short), with at least two tiles per consumer warp.
 Plan make_plan(int b, int hq, int hkv, int d, int max_blocks, int n_shared) {
   Plan pl{};
   pl.n_shared_ctas_per_head = (n_shared + kChunk - 1) / kChunk;
+  const int row_tiles = (b * (hq / hkv) + 15) / 16;
+  pl.n_row_groups = (row_tiles + kCons - 1) / kCons;
   const int priv_max = max_blocks - n_shared > 0 ? max_blocks - n_shared : 1;
   const int pairs = b * hkv;
-  const int target = 3 * sm_count_attn() - pl.n_shared_ctas_per_head * hkv;
+  const int target = 15 * sm_count_attn() / 2 - pl.n_shared_ctas_per_head * pl.n_row_groups * hkv;
   int nsplit = target > pairs ? (target + pairs - 1) / pairs : 1;
-  const int max_split = (priv_max + kWarps - 1) / kWarps;
+  const int max_split = (priv_max + 2 * kCons - 1) / (2 * kCons);
   nsplit = nsplit > max_split ? max_split : nsplit;
   nsplit = nsplit < 1 ? 1 : nsplit;
   pl.bps = (priv_max + nsplit - 1) / nsplit;
@@ -411,16 +558,37 @@ Plan make_plan(int b, int hq, int hkv, int d, int max_blocks, int n_shared) {
 }
 
 template <int D>
-int launch_attn(AttnParams& p, const Plan& pl, cudaStream_t st) {
+int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v_pool, cudaStream_t st) {
+  using C = AttnCfg<D>;
   static bool attr_done = false;
   if (!attr_done) {
-    MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     AttnCfg<D>::kSmem));
+    MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::kSmem));
+    MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::kSmem));
     attr_done = true;
   }
-  const int64_t ctas = (int64_t)pl.n_shared_ctas_per_head * p.hkv + (int64_t)p.b * p.hkv * pl.nsplit;
+  // Pools as 2-D tensors [num_blocks*hkv*16 rows, D]: rows of one (block, kv head) tile are adjacent.
+  const uint64_t rows = (uint64_t)p.num_blocks * p.hkv * 16;
+  if (rows > 0x7fffffffull) return MG_ERR_UNSUPPORTED;
+  const CUtensorMapSwizzle sw = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUtensorMap tk, tv;
+  int rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
+  if (rc) return rc;
+  rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, v_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
+  if (rc) return rc;
+  p.n_shared_ctas_per_head = pl.n_shared_ctas_per_head;
+  p.n_row_groups = pl.n_row_groups;
+  const int64_t ctas = (int64_t)pl.n_shared_ctas_per_head * pl.n_row_groups * p.hkv +
+                       (int64_t)p.b * p.hkv * pl.nsplit;
   if (ctas > 0x7fffffff) return MG_ERR_UNSUPPORTED;
-  MG_CUDA_TRY(mg_launch(paged_attn_kernel<D>, dim3((unsigned)ctas), dim3(kThreads), AttnCfg<D>::kSmem, st, 1, p));
+  if (p.group <= 8) {
+    MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, true>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk, tv,
+                          p));
+  } else {
+    MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, false>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk,
+                          tv, p));
+  }
   if (!pl.direct) {
     MG_CUDA_TRY(mg_launch(combine_kernel<D>, dim3((unsigned)(p.b * p.hq)), dim3(D), 0, st, 1, p.ws_o, p.ws_ml,
                           pl.nslots, p.out));
@@ -456,8 +624,6 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
     return MG_ERR_INVALID_ARG;
   AttnParams p{};
   p.q = q;
-  p.kp = static_cast<const __nv_bfloat16*>(k_pool);
-  p.vp = static_cast<const __nv_bfloat16*>(v_pool);
   p.num_blocks = num_blocks;
   p.tables = block_tables;
   p.max_blocks = max_blocks;
@@ -477,8 +643,8 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
   p.ws_ml = pl.ws_bytes ? static_cast<float*>(workspace) + (size_t)b * hq * pl.nslots * d : nullptr;
   p.direct = pl.direct;
   cudaStream_t st = mg_stream(stream);
-  if (d == 32) return launch_attn<32>(p, pl, st);
-  return d == 64 ? launch_attn<64>(p, pl, st) : launch_attn<128>(p, pl, st);
+  if (d == 32) return launch_attn<32>(p, pl, k_pool, v_pool, st);
+  return d == 64 ? launch_attn<64>(p, pl, k_pool, v_pool, st) : launch_attn<128>(p, pl, k_pool, v_pool, st);
 }
 
 // ------------------------------------------------------------------------------------------------

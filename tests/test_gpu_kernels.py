@@ -277,6 +277,22 @@ def test_paged_attention_shared_prefix_equals_unshared():
     close(a, b_, rtol=1e-2, atol=5e-3)
 
 
+@pytest.mark.parametrize("n_shared", [0, 2])
+def test_paged_attention_ignores_nan_in_unused_slots(n_shared):
+    """Pool slots past a sequence's length hold whatever was there (NaN here); the partial last block
+    is read whole by TMA and its unused V rows must not leak into the output."""
+    ctx = [37, 16 * 5 + 1, 200, 16 * 3]
+    q, kp, vp, tables, ctxa = _paged_case(4, 24, 8, 128, ctx, n_shared, seed=11)
+    for i, c in enumerate(ctxa):
+        if c % 16:
+            last = tables[i, (c - 1) // 16]
+            kp[last, :, c % 16:, :] = np.nan
+            vp[last, :, c % 16:, :] = np.nan
+    got = _run_attn(q, kp, vp, tables, ctxa, n_shared)
+    assert np.isfinite(got).all()
+    close(got, oatt.paged_decode_attention(q, kp, vp, tables, ctxa, 1.0 / np.sqrt(128)))
+
+
 def test_no_device_error_recorded():
     K().check_device()
 
