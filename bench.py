@@ -55,6 +55,66 @@ def parse():
     return ap.parse_args()
 
 
+def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps: int = 10) -> dict:
+    """Device time of each hot kernel family on its own: one CUDA graph holding every launch of that
+    family in a decode step (the step's weights, pools, shapes and epilogues, back to back as in the
+    step; residual adds go to a scratch buffer), replayed ``reps`` times between CUDA events on the
+    launch stream. Per family: launches, microseconds per step and per launch, algorithmic bytes
+    (INT8 codes + scales + activations in/out; K/V bytes read) and GB/s."""
+    import torch
+    from microgen_b200 import kernels as K
+    w, H = eng.w, spec.hidden
+    scratch = torch.zeros((b, H), dtype=torch.float32, device=eng.h.device)
+    nqkv = (eng.hq + 2 * eng.hkv) * eng.D
+    epi_mlp = K.EPI_GELU_BF16 if spec.family == "gpt2" else K.EPI_SWIGLU_BF16
+    lin = []  # (x, q, s, bias, y, epilogue, bytes)
+    for L in w.layers:
+        lin.append((eng.x[:b], L.qkv_q, L.qkv_s, L.qkv_b, eng.qkv[:b], K.EPI_STORE_F32,
+                    eng.linear_bytes(L.qkv_q, b, 4, nqkv)))
+        lin.append((eng.attn[:b], L.o_q, L.o_s, None, scratch, K.EPI_ADD_F32, eng.linear_bytes(L.o_q, b, 8, H)))
+        lin.append((eng.x[:b], L.gu_q, L.gu_s, L.gu_b, eng.act[:b], epi_mlp,
+                    eng.linear_bytes(L.gu_q, b, 2, eng.act.shape[1])))
+        lin.append((eng.act[:b], L.d_q, L.d_s, None, scratch, K.EPI_ADD_F32, eng.linear_bytes(L.d_q, b, 8, H)))
+    lin.append((eng.x[:b], w.lm_q, w.lm_s, None, eng.logits[:b], K.EPI_STORE_F32,
+                eng.linear_bytes(w.lm_q, b, 4, spec.vocab)))
+    tab, ctx = eng.tables[:b], eng.ctx[:b]
+    attn_bytes = kv_tokens * eng.hkv * eng.D * 2 * 2 + b * eng.hq * eng.D * (4 + 2)
+
+    def run_lin():
+        for x, q, sc, bias, y, e, _ in lin:
+            K.i8_linear(x, q, sc, bias, y=y, epilogue=e)
+
+    def run_attn():
+        for l in range(len(w.layers)):
+            K.paged_decode_attn(eng.q[:b], eng.pool.k[l], eng.pool.v[l], tab, ctx, eng.scale,
+                                n_shared_blocks=n_shared_blocks, out=eng.attn[:b], workspace=eng.workspace)
+
+    out = {}
+    for name, fn, n, nbytes in (("i8_linear", run_lin, len(lin), sum(t[-1] for t in lin)),
+                                ("paged_attn", run_attn, len(w.layers), attn_bytes * len(w.layers))):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        out[name] = {"launches_per_step": n, "us_per_step": round(us, 2), "us_per_launch": round(us / n, 3),
+                     "bytes_per_launch": int(nbytes // n), "gbs": round(nbytes / us / 1e3, 1),
+                     "timing": f"CUDA graph of the step's {n} {name} launches, {reps} replays, CUDA events"}
+    K.check_device()
+    return out
+
+
 def peaks() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -337,19 +397,21 @@ def main():
         kernels[kind] = {"launches_per_step": len(recs) // 3, "us_per_step": round(tsum / 3 * 1e6, 2),
                          "gbs": round(bsum / tsum / 1e9, 1)}
     hbm, hbm_kind = peaks()
-    dom = max(("paged_attn", "i8_linear"), key=lambda k: kernels.get(k, {}).get("us_per_step", 0.0))
-    recs = stats[dom]
-    t_dom = sum(a.elapsed_time(b) for a, b, _ in recs) / 1e3
-    achieved = sum(n for _, _, n in recs) / t_dom / 1e9
+    log("kernel chains")
+    chains = kernel_chains(eng, spec, B, cache.n_shared_blocks, kv_tokens)
+    dom = max(chains, key=lambda k: chains[k]["us_per_step"])
+    achieved = chains[dom]["gbs"]
     traffic = None
-    tr_path = os.path.join(ROOT, "profiles", "traffic_per_launch.json")
+    tr_path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
     if os.path.exists(tr_path):
         try:
             traffic = json.load(open(tr_path)).get(f"{args.workload}:{dom}")
         except Exception:
             traffic = None
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": hbm_kind}
+                "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": hbm_kind,
+                "algorithmic_bytes_per_launch": chains[dom]["bytes_per_launch"],
+                "us_per_launch": chains[dom]["us_per_launch"], "timing": chains[dom]["timing"]}
     step_bytes = eng.w.int8_bytes() + kv_tokens * eng.hkv * spec.head_dim * 2 * 2 * spec.layers
     step_roofline = {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms / 1e3) / 1e9, 1),
                      "frac": round(step_bytes / (ms / 1e3) / 1e9 / hbm, 4)}
@@ -409,7 +471,7 @@ def main():
                    "batch": B, "prompt": P, "shared_prefix": S, "tp": world, "parallelism": f"tp{world}",
                    "l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True,
                    "row_parallel_reduce": reduce_kind},
-        "roofline": roofline, "step_roofline": step_roofline, "kernels": kernels,
+        "roofline": roofline, "step_roofline": step_roofline, "kernel_chains": chains, "kernels": kernels,
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst,
         "clocks": clk.summary(), "setup_s": {"load": round(t_load, 1), "prefill": round(t_prefill, 1)},
     }
