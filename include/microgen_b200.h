@@ -84,13 +84,13 @@ int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t ldx, const 
 
 /* ---- fused row-parallel all-reduce over peer memory (parallel.py:65-81 + its "all-reduce") ---------
  * One communicator per rank of a tensor-parallel group (world <= 8, one process per GPU):
- *   mg_comm_create  allocates this rank's receive area (2 sets x world x slot_elems 64-bit words) and
+ *   mg_comm_create  allocates this rank's receive area (2 sets x world x slot_elems/2 64-bit words) and
  *                   writes its CUDA IPC handle (mg_comm_handle_bytes() bytes) to ipc_handle;
  *   mg_comm_open    maps every rank's area from the world handles (rank order, concatenated);
  *   mg_comm_destroy unmaps and frees.
  * mg_i8_linear_packed_rowpar runs this rank's partial of a row-parallel linear (tile-packed codes, scale
  * applied, no bias) and its epilogue stores each output tile straight into every rank's receive slot over
- * NVLink as words {fp32 value, all-reduce epoch}. mg_rowpar_reduce_norm waits (at most about 1 s, then
+ * NVLink as words {two bf16 values, all-reduce epoch} (n % 128 == 0). mg_rowpar_reduce_norm waits (at most about 1 s, then
  * MG_ERR_TIMEOUT in the device error word) until every word it sums carries the current epoch, sets
  * h += sum over ranks (rank order) +
  * bias, and with norm = 1 (RMSNorm, w) or 2 (LayerNorm, w, wb) writes x = bf16(norm(h)). Every rank must

@@ -2,8 +2,8 @@
 //
 // The push half lives in the tcgen05 linear's MG_EPI_PEER_F32 epilogue (i8_linear.cu): every CTA
 // stores its output tile (scale applied, no bias) into slot [e%2][my rank] of every rank's receive
-// area over NVLink as 64-bit words {fp32 value, epoch e}; the last CTA of the launch advances this
-// rank's count to e.
+// area over NVLink as 64-bit words {two bf16 values, epoch e}; the last CTA of the launch advances
+// this rank's count to e.
 //
 // rowpar_reduce_norm_kernel reads e from the count, waits (bounded by time) until each word it
 // needs carries epoch e, sums the world partials in rank order onto the fp32 residual (identical
@@ -49,16 +49,13 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return red[0];
 }
 
-// Waits until the four words at p carry `epoch` (16-byte aligned). Gives up once `dead` is set or
-// the wait has run for kWaitNs, recording MG_ERR_TIMEOUT with the peer rank in the detail.
-__device__ __forceinline__ void wait_words(const uint64_t* p, uint32_t epoch, uint64_t (&wd)[4], uint64_t& t0,
+// Waits until the two words at p (four values, 16-byte aligned) carry `epoch`. Gives up once `dead`
+// is set or the wait has run for kWaitNs, recording MG_ERR_TIMEOUT with the peer rank in the detail.
+__device__ __forceinline__ void wait_words(const uint64_t* p, uint32_t epoch, uint64_t (&wd)[2], uint64_t& t0,
                                            bool& dead, int r) {
   for (uint32_t spin = 0;; ++spin) {
     ld_volatile_v2u64(p, wd[0], wd[1]);
-    ld_volatile_v2u64(p + 2, wd[2], wd[3]);
-    if (dead || ((uint32_t)(wd[0] >> 32) == epoch && (uint32_t)(wd[1] >> 32) == epoch &&
-                 (uint32_t)(wd[2] >> 32) == epoch && (uint32_t)(wd[3] >> 32) == epoch))
-      return;
+    if (dead || ((uint32_t)(wd[0] >> 32) == epoch && (uint32_t)(wd[1] >> 32) == epoch)) return;
     if ((spin & 31) == 31) {
       const uint64_t t = global_ns();
       if (t0 == 0) {
@@ -84,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
   griddep_wait();
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(po.count);
   const int64_t row = blockIdx.x;
-  const uint64_t* recv = po.recv[po.rank] + (int64_t)(epoch & 1u) * po.world * po.slot + row * n;
+  const uint64_t* recv = po.recv[po.rank] + (int64_t)(epoch & 1u) * po.world * po.slot + row * (n / 2);
   float* hr = h + row * n;
   const int nv = n >> 2;
   uint64_t t0 = 0;
@@ -97,12 +94,12 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
     if (idx < nv) {
       float4 a = reinterpret_cast<const float4*>(hr)[idx];
       for (int r = 0; r < po.world; ++r) {
-        uint64_t wd[4];
-        wait_words(recv + (int64_t)r * po.slot + idx * 4, epoch, wd, t0, dead, r);
-        a.x += __uint_as_float((uint32_t)wd[0]);
-        a.y += __uint_as_float((uint32_t)wd[1]);
-        a.z += __uint_as_float((uint32_t)wd[2]);
-        a.w += __uint_as_float((uint32_t)wd[3]);
+        uint64_t wd[2];
+        wait_words(recv + (int64_t)r * po.slot + idx * 2, epoch, wd, t0, dead, r);
+        a.x += bf16lo((uint32_t)wd[0]);
+        a.y += bf16hi((uint32_t)wd[0]);
+        a.z += bf16lo((uint32_t)wd[1]);
+        a.w += bf16hi((uint32_t)wd[1]);
       }
       if (bias) {
         const float4 b = reinterpret_cast<const float4*>(bias)[idx];
@@ -179,7 +176,7 @@ extern "C" int mg_comm_create(int rank, int world, int64_t slot_elems, void** co
   Comm* c = new Comm();
   c->rank = rank;
   c->world = world;
-  c->slot = (slot_elems + 63) / 64 * 64;
+  c->slot = ((slot_elems + 1) / 2 + 63) / 64 * 64;  // words of two values
   c->recv_bytes = align_up((size_t)2 * world * c->slot * sizeof(uint64_t), 256);
   c->bytes = c->recv_bytes + 256;  // + the two local counters
   cudaError_t e = cudaGetDevice(&c->device);
@@ -235,7 +232,7 @@ extern "C" int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, in
   PeerOut po;
   int rc = mg_comm_peer_out(comm, &po);
   if (rc) return rc;
-  if (!h || m < 0 || n <= 0 || n % 4 || n > 4 * kThreads * kMaxV || (int64_t)m * n > po.slot || norm < 0 ||
+  if (!h || m < 0 || n <= 0 || n % 4 || n > 4 * kThreads * kMaxV || (int64_t)m * n > 2 * po.slot || norm < 0 ||
       norm > 2 || (norm && (!w || !x)) || (norm == 2 && !wb))
     return MG_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(w) |

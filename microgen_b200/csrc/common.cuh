@@ -82,9 +82,10 @@ static inline cudaError_t mg_launch(void (*kernel)(KArgs...), dim3 grid, dim3 bl
 // Every rank owns one device allocation, mapped into every other rank's process through CUDA IPC:
 //   recv  u64 [2 sets][world][slot]   rank r's partial of all-reduce e lands in set e%2, slot r
 // plus two local counters (all-reduces pushed by this rank; CTAs done in the push under way).
-// Each receive word carries its own flag: low half = the fp32 partial, high half = the epoch e
-// of the all-reduce that wrote it. An aligned 64-bit store is single-copy atomic, so a reader
-// that sees epoch e in a word also sees that word's value; no fence or separate flag is needed.
+// Each receive word carries its own flag: low half = two adjacent partial values as bf16 (the
+// precision the reference's all-reduce of bf16 linear outputs has), high half = the epoch e of the
+// all-reduce that wrote it. An aligned 64-bit store is single-copy atomic, so a reader that sees
+// epoch e in a word also sees that word's values; no fence or separate flag is needed.
 // ---------------------------------------------------------------------------------------------
 #define MG_MAX_RANKS 8
 #define MG_EPI_PEER_F32 5  // internal epilogue: push acc*scale to every rank's receive slot
@@ -93,7 +94,7 @@ struct PeerOut {
   uint64_t* recv[MG_MAX_RANKS];    // each rank's receive area, as mapped in this process
   uint32_t* count;                 // this rank: all-reduces pushed so far (= epoch of the last one)
   uint32_t* done;                  // this rank: CTAs finished in the push under way
-  int64_t slot;                    // words per (set, rank) slot
+  int64_t slot;                    // words (value pairs) per (set, rank) slot
   int rank, world;
 };
 

@@ -482,10 +482,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int ml0 = (int)crank + half * split;
     auto emit = [&](int ml, float a0, float a1) {
       const int m = m_base + ml;
-      if (peer) {
-        const uint64_t word = tag | __float_as_uint(a0 * s0);
-        const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + (int64_t)m * N + n0;
-        for (int r = 0; r < po.world; ++r) st_volatile_u64(po.recv[r] + off, word);
+      if (peer) {  // warp-uniform (N % 128 == 0): lane pairs (n, n+1) share one word
+        const float v = a0 * s0;
+        const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
+        if ((n0 & 1) == 0) {
+          const uint64_t word = tag | pack_bf16x2(v, v1);
+          const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + ((int64_t)m * N + n0) / 2;
+          for (int r = 0; r < po.world; ++r) st_volatile_u64(po.recv[r] + off, word);
+        }
       } else if (epi == MG_EPI_ADD_F32) {
         red_add_f32(static_cast<float*>(y) + (int64_t)m * ldy + n0, a0 * s0 + b0);
       } else if (!swiglu) {
@@ -689,8 +693,9 @@ extern "C" int mg_i8_linear_packed_rowpar(const void* x, int64_t m, int64_t k, i
   PeerOut po;
   int rc = mg_comm_peer_out(comm, &po);
   if (rc) return rc;
-  if (m < 0 || k <= 0 || n <= 0 || !x || !packed || !scales || k % 16 || ldx < k || ldx % 8 || split_k < 0 ||
-      split_k > 8 || m * n > po.slot || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(packed)) & 15))
+  if (m < 0 || k <= 0 || n <= 0 || !x || !packed || !scales || k % 16 || n % 128 || ldx < k || ldx % 8 ||
+      split_k < 0 || split_k > 8 || m * n > 2 * po.slot ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(packed)) & 15))
     return MG_ERR_INVALID_ARG;
   if (k > 0x7fffffff || m > 0x7fffffff) return MG_ERR_UNSUPPORTED;
   if (m == 0) return MG_OK;

@@ -1,7 +1,7 @@
 """Fused row-parallel all-reduce on one GPU (the multi-GPU path is tests/test_gpu_tp.py).
 
 * world 1: the row-parallel push + reduce(+norm) equals ``h + x·(q·s)ᵀ + bias`` and the RMSNorm /
-  LayerNorm of it, against the fp64 oracle;
+  LayerNorm of it, against the fp64 oracle (partials travel as bf16: the contract's bf16 tolerance);
 * a missing peer: a world-2 communicator whose second rank never pushes — the reduce kernel's
   bounded wait gives up after about a second, records MG_ERR_TIMEOUT, and the host raises
   TimeoutError; the context stays usable (a later world-1 reduce still works).
@@ -52,7 +52,7 @@ def test_world1_push_reduce_norm(norm):
             xo = K.rowpar_reduce_norm(comm, h, d(bias), norm, d(g), d(gb), 1e-5)
             torch.cuda.synchronize()
             want_h = h0 + olin.i8_linear(x.float().numpy(), q, s, bias)
-            _close(h.cpu().numpy(), want_h, 1e-4, 1e-4)
+            _close(h.cpu().numpy(), want_h, 2e-2, 1e-2)  # partials travel as bf16
             if norm == 1:
                 want_x = g * (want_h / np.sqrt((want_h ** 2).mean(-1, keepdims=True) + 1e-5))
                 _close(xo.float().cpu().numpy(), want_x, 2e-2, 1e-2)
