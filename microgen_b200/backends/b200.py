@@ -30,7 +30,7 @@ import torch.nn as nn
 from .. import kernels as K
 from ..engine import DecodeEngine, WeightLoader
 from ..model_spec import spec_from_hf_config
-from ..runtime.paged_kv import BlockTable, PagedKVCacheAllocator
+from ..runtime.paged_kv import BlockTable, PagedKVCacheAllocator, TableMirror
 
 BLOCK = 16
 
@@ -64,6 +64,7 @@ class PagedKVCache:
         self.tables: List[BlockTable] = []
         self.prefix: Optional[BlockTable] = None
         self.n_shared_blocks = 0
+        self.mirror: Optional[TableMirror] = None  # host copy of the block tables for decode steps
 
     def __bool__(self) -> bool:
         return True
@@ -155,7 +156,7 @@ class B200QuantizedBackend:
         return t.detach().to("cpu", torch.int64).tolist()
 
     def _run(self, tables: List[BlockTable], tokens: List[int], positions: List[int], n_shared: int,
-             logits: bool) -> None:
+             logits: bool, cache_mirror: Optional[TableMirror] = None) -> None:
         eng = self.engine
         b = len(tables)
         slots = [t.slot(p) for t, p in zip(tables, positions)]
@@ -163,10 +164,9 @@ class B200QuantizedBackend:
         width = max(t.num_blocks() for t in tables)
         if width > eng.max_blocks:
             raise ValueError(f"context of {width * BLOCK} tokens exceeds max_seq_len {self.max_seq_len}")
-        tab = torch.zeros((b, width), dtype=torch.int32)
-        for i, t in enumerate(tables):
-            ids = t.block_ids()
-            tab[i, : len(ids)] = torch.tensor(ids, dtype=torch.int32)
+        if cache_mirror is None:
+            cache_mirror = TableMirror(b, eng.max_blocks)
+        tab = torch.from_numpy(cache_mirror.update(tables))
         eng.set_inputs(tokens, positions, slots, ctx, tab)
         if self.use_cuda_graph:
             eng.capture(b, n_shared, compute_logits=logits).replay()
@@ -193,8 +193,9 @@ class B200QuantizedBackend:
                 n_shared = min(lcp, T - 1) // BLOCK if b > 1 else 0
                 if n_shared:
                     cache.prefix = self.allocator.allocate_sequence("prefix", n_shared * BLOCK)
+                    prefix_mirror = TableMirror(1, eng.max_blocks)
                     for p in range(n_shared * BLOCK):
-                        self._run([cache.prefix], [ids[0][p]], [p], 0, logits=False)
+                        self._run([cache.prefix], [ids[0][p]], [p], 0, logits=False, cache_mirror=prefix_mirror)
                     cache.tables = [self.allocator.share_prefix(cache.prefix, n_shared, f"seq{i}", T)
                                     for i in range(b)]
                     start = n_shared * BLOCK
@@ -210,8 +211,11 @@ class B200QuantizedBackend:
                         self.allocator.append_token(t)
                 ids = [[0] * start + r for r in ids]
                 T = start + T
+            if cache.mirror is None or cache.mirror.arr.shape[0] < b:
+                cache.mirror = TableMirror(b, eng.max_blocks)
             for p in range(start, T):
-                self._run(cache.tables, [r[p] for r in ids], [p] * b, cache.n_shared_blocks, logits=(p == T - 1))
+                self._run(cache.tables, [r[p] for r in ids], [p] * b, cache.n_shared_blocks, logits=(p == T - 1),
+                          cache_mirror=cache.mirror)
             return eng.logits[:b].clone(), cache
 
     def decode(self, token_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
@@ -228,7 +232,9 @@ class B200QuantizedBackend:
             for t in cache.tables:
                 positions.append(t.num_tokens)
                 self.allocator.append_token(t)
-            self._run(cache.tables, toks, positions, cache.n_shared_blocks, logits=True)
+            if cache.mirror is None or cache.mirror.arr.shape[0] < b:
+                cache.mirror = TableMirror(b, eng.max_blocks)
+            self._run(cache.tables, toks, positions, cache.n_shared_blocks, logits=True, cache_mirror=cache.mirror)
             return eng.logits[:b].clone(), cache
 
     def sample(self, logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0,

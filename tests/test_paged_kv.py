@@ -1,0 +1,105 @@
+"""Paged block allocator (CPU): the reference's block-id order, its error behaviour, the additions for
+the device path (rollback, shared prefixes) and the incremental host mirror of the block tables."""
+
+import json
+import os
+import random
+
+import numpy as np
+import pytest
+
+from microgen_b200.runtime.paged_kv import PagedKVCacheAllocator, TableMirror, block_table_tensor
+
+G = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_allocator_replays_reference_trace():
+    """Same operations as tests/golden/make_golden.py ran on the reference allocator: identical block
+    ids at every step, identical free list after a free, identical out-of-memory message."""
+    want = json.load(open(os.path.join(G, "alloc_trace.json")))
+    a = PagedKVCacheAllocator(num_blocks=12, block_size=16)
+    got = []
+    t1 = a.allocate_sequence("a", 35)
+    got.append(["alloc", "a", 35, [b.block_id for b in t1.physical_blocks]])
+    t2 = a.allocate_sequence("b", 16)
+    got.append(["alloc", "b", 16, [b.block_id for b in t2.physical_blocks]])
+    for _ in range(13):
+        a.append_token(t1)
+    got.append(["append13", "a", t1.num_tokens, [b.block_id for b in t1.physical_blocks]])
+    a.append_token(t2)
+    got.append(["append1", "b", t2.num_tokens, [b.block_id for b in t2.physical_blocks]])
+    a.free_sequence(t1)
+    got.append(["free", "a", a.get_num_free_blocks(), [b.block_id for b in a._free_blocks]])
+    t3 = a.allocate_sequence("c", 70)
+    got.append(["alloc", "c", 70, [b.block_id for b in t3.physical_blocks]])
+    t4 = a.allocate_sequence("d", 0)
+    got.append(["alloc", "d", 0, [b.block_id for b in t4.physical_blocks]])
+    with pytest.raises(MemoryError) as e:
+        a.allocate_sequence("e", 16 * 20)
+    got.append(["oom", "e", 320, str(e.value)])
+    assert got == want
+
+
+def test_block_counts_overflow_and_oom():
+    a = PagedKVCacheAllocator(num_blocks=4)
+    t = a.allocate_sequence("s", 16)
+    assert t.num_blocks() == 1 and a.get_num_free_blocks() == 3
+    a.append_token(t)  # 17th token opens a second block
+    assert t.num_blocks() == 2 and t.slot(16) == t.physical_blocks[1].block_id * 16
+    a.allocate_sequence("u", 32)
+    with pytest.raises(MemoryError):
+        a.allocate_sequence("v", 1)
+    a.free_sequence(t)
+    assert a.get_num_free_blocks() == 2 and t.num_blocks() == 0
+
+
+def test_rollback_and_shared_prefix_refcounts():
+    a = PagedKVCacheAllocator(num_blocks=16)
+    src = a.allocate_sequence("p", 40)  # 3 blocks, 2 full
+    s1 = a.share_prefix(src, 2, "s1", 40)
+    s2 = a.share_prefix(src, 2, "s2", 50)
+    assert s1.block_ids()[:2] == s2.block_ids()[:2] == src.block_ids()[:2]
+    assert src.physical_blocks[0].ref_count == 3
+    v = s2.version
+    a.rollback(s2, 30)  # 50 -> 20 tokens: two blocks left, the shared ones
+    assert s2.num_tokens == 20 and s2.num_blocks() == 2 and s2.version > v
+    a.free_sequence(s1)
+    a.free_sequence(s2)
+    assert src.physical_blocks[0].ref_count == 1  # still held by the source
+    with pytest.raises(ValueError):
+        a.share_prefix(src, 3, "bad", 48)  # the third block is not full
+
+
+def test_table_mirror_tracks_appends_rollbacks_and_replacements():
+    rng = random.Random(0)
+    a = PagedKVCacheAllocator(num_blocks=4000)
+    a.shuffle_free_list(1)
+    tables = [a.allocate_sequence(f"s{i}", rng.randint(1, 300)) for i in range(12)]
+    m = TableMirror(12, 64)
+    for step in range(400):
+        op = rng.random()
+        i = rng.randrange(len(tables))
+        if op < 0.85:
+            for t in tables:
+                a.append_token(t)
+        elif op < 0.93:
+            a.rollback(tables[i], rng.randint(1, 60))
+        elif op < 0.97:
+            a.free_sequence(tables[i])
+            tables[i] = a.allocate_sequence(f"r{step}", rng.randint(1, 200))
+        else:
+            a.free_sequence(tables[i])
+            a.append_token(tables[i])
+        got = m.update(tables)
+        width = max(t.num_blocks() for t in tables)
+        want = block_table_tensor(tables, 64).numpy()[:, :width]
+        assert got.shape == want.shape and np.array_equal(got, want), f"step {step}"
+
+
+def test_table_mirror_rejects_oversized_input():
+    a = PagedKVCacheAllocator(num_blocks=64)
+    m = TableMirror(2, 4)
+    with pytest.raises(ValueError):
+        m.update([a.allocate_sequence("x", 16 * 5)])
+    with pytest.raises(ValueError):
+        m.update([a.allocate_sequence(f"y{i}", 1) for i in range(3)])
