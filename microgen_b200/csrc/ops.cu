@@ -213,31 +213,58 @@ __global__ void rope_kv_append_kernel(const float* __restrict__ qkv, int64_t ld_
   dst[j + half] = __float2bfloat16_rn(b);
 }
 
-// torch.argmax semantics: the first index holding the maximum.
-__global__ void argmax_kernel(const float* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ out) {
-  griddep_launch();
-  griddep_wait();
-  __shared__ float sv[32];
-  __shared__ int32_t si[32];
-  const float* r = logits + (int64_t)blockIdx.x * ld;
-  float best = -INFINITY;
-  int32_t bi = 0x7fffffff;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = r[i];
-    if (v > best) {
-      best = v;
-      bi = (int32_t)i;
-    }
+// torch.argmax semantics: the first index holding the maximum. A row is split over a cluster of
+// kArgSplit CTAs (contiguous chunks, float4 loads where the row is 16-byte aligned); CTA 0 of the
+// cluster merges the chunk results through distributed shared memory, smaller index on ties.
+constexpr int kArgSplit = 8;
+constexpr int kArgThreads = 512;
+
+__device__ __forceinline__ void argmax_take(float v, int32_t i, float& best, int32_t& bi) {
+  if (v > best || (v == best && i < bi)) {
+    best = v;
+    bi = i;
   }
+}
+
+__device__ __forceinline__ void warp_argmax(float& best, int32_t& bi) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
     const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
+    argmax_take(ov, oi, best, bi);
   }
+}
+
+__global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* __restrict__ logits, int64_t n, int64_t ld,
+                                                             int32_t* __restrict__ out) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int32_t si[kArgThreads / 32];
+  __shared__ float cta_best;
+  __shared__ int32_t cta_idx;
+  const int part = (int)blockIdx.x;  // rank in the cluster
+  const float* r = logits + (int64_t)blockIdx.y * ld;
+  const int64_t chunk = ((n + kArgSplit - 1) / kArgSplit + 3) / 4 * 4;
+  const int64_t lo = (int64_t)part * chunk, hi = lo + chunk < n ? lo + chunk : n;
+  float best = -INFINITY;
+  int32_t bi = 0x7fffffff;
+  int64_t i0 = lo;
+  if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && hi > lo) {  // lo is a multiple of 4
+    const int64_t nv = (hi - lo) >> 2;
+    const float4* r4 = reinterpret_cast<const float4*>(r + lo);
+    for (int64_t j = threadIdx.x; j < nv; j += kArgThreads) {
+      const float4 v = r4[j];
+      const int32_t k = (int32_t)(lo + 4 * j);
+      if (v.x > best) { best = v.x; bi = k; }
+      if (v.y > best) { best = v.y; bi = k + 1; }
+      if (v.z > best) { best = v.z; bi = k + 2; }
+      if (v.w > best) { best = v.w; bi = k + 3; }
+    }
+    i0 = lo + 4 * nv;
+  }
+  for (int64_t i = i0 + threadIdx.x; i < hi; i += kArgThreads) argmax_take(r[i], (int32_t)i, best, bi);
+  warp_argmax(best, bi);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   if (l == 0) {
     sv[w] = best;
@@ -245,20 +272,26 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int64_t n, int64
   }
   __syncthreads();
   if (w == 0) {
-    const int nw = blockDim.x >> 5;
-    best = l < nw ? sv[l] : -INFINITY;
-    bi = l < nw ? si[l] : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi)) {
-        best = ov;
-        bi = oi;
-      }
+    best = l < kArgThreads / 32 ? sv[l] : -INFINITY;
+    bi = l < kArgThreads / 32 ? si[l] : 0x7fffffff;
+    warp_argmax(best, bi);
+    if (l == 0) {
+      cta_best = best;
+      cta_idx = bi;
     }
-    if (l == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
   }
+  cluster_sync_all();
+  if (part == 0 && w == 0) {
+    best = -INFINITY;
+    bi = 0x7fffffff;
+    if (l < kArgSplit) {
+      best = ld_dsmem_f32(mapa_shared(smem_u32(&cta_best), (uint32_t)l));
+      bi = __float_as_int(ld_dsmem_f32(mapa_shared(smem_u32(&cta_idx), (uint32_t)l)));
+    }
+    warp_argmax(best, bi);
+    if (l == 0) out[blockIdx.y] = bi == 0x7fffffff ? 0 : bi;
+  }
+  cluster_sync_all();  // the other CTAs' results stay readable until CTA 0 has read them
 }
 
 __global__ void decode_advance_kernel(int32_t* tokens, const int32_t* next_tokens, int32_t* positions,
@@ -346,7 +379,9 @@ extern "C" int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t
 extern "C" int mg_argmax_rows(const float* logits, int m, int64_t n, int64_t ld, int32_t* out, void* stream) {
   if (m < 0 || n <= 0 || ld < n || !logits || !out || n > 0x7fffffff) return MG_ERR_INVALID_ARG;
   if (m == 0) return MG_OK;
-  MG_CUDA_TRY(mg_launch(argmax_kernel, dim3(m), dim3(1024), 0, mg_stream(stream), 1, logits, n, ld, out));
+  if (m > 65535) return MG_ERR_UNSUPPORTED;
+  MG_CUDA_TRY(mg_launch(argmax_kernel, dim3(kArgSplit, m), dim3(kArgThreads), 0, mg_stream(stream), kArgSplit, logits,
+                        n, ld, out));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }

@@ -211,8 +211,23 @@ def test_argmax_first_max_index():
     lg[1, 77] = lg[1, 1000] = 50.0     # tie -> first index
     lg[2, :] = 0.0
     lg[3, -1] = 99.0
+    lg[4, 5] = lg[4, 100000] = 60.0    # tie across the row's chunks
+    lg[5, 128255] = 70.0               # last element
     out = K().argmax_rows(dev(lg)).cpu().numpy()
     assert out.tolist() == np.argmax(lg, axis=1).tolist()
+
+
+@pytest.mark.parametrize("n,ld", [(5, 5), (31, 33), (1000, 1003), (50257, 50257), (50257, 50260)])
+def test_argmax_short_and_unaligned_rows(n, ld):
+    """Rows shorter than the split, and rows whose stride breaks 16-byte alignment (scalar path)."""
+    rng = np.random.default_rng(n)
+    full = rng.standard_normal((9, ld)).astype(np.float32)
+    full[0, n - 1] = 40.0
+    full[1, 0] = 40.0
+    full[2, :n] = 1.0
+    lgd = dev(full)[:, :n]
+    out = K().argmax_rows(lgd).cpu().numpy()
+    assert out.tolist() == np.argmax(full[:, :n], axis=1).tolist()
 
 
 # ------------------------------------------------------------------ paged attention
