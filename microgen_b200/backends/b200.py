@@ -166,7 +166,7 @@ class B200QuantizedBackend:
             raise ValueError(f"context of {width * BLOCK} tokens exceeds max_seq_len {self.max_seq_len}")
         if cache_mirror is None:
             cache_mirror = TableMirror(b, eng.max_blocks)
-        tab = torch.from_numpy(cache_mirror.update(tables))
+        tab = cache_mirror.update(tables)
         eng.set_inputs(tokens, positions, slots, ctx, tab)
         if self.use_cuda_graph:
             eng.capture(b, n_shared, compute_logits=logits).replay()

@@ -28,6 +28,7 @@ import os
 from dataclasses import dataclass, field
 from typing import Optional
 
+import numpy as np
 import torch
 
 from . import kernels as K
@@ -246,11 +247,12 @@ class DecodeEngine:
             self.cos_sin = rope_table(self.D, spec.rope_theta, max(max_pos, self.max_ctx)).to(dev)
         B, H = max_batch, spec.hidden
         i32 = dict(dtype=torch.int32, device=dev)
-        self.tokens = torch.zeros(B, **i32)
-        self.positions = torch.zeros(B, **i32)
-        self.slots = torch.zeros(B, **i32)
-        self.ctx = torch.ones(B, **i32)
-        self.tables = torch.zeros((B, max_blocks_per_seq), **i32)
+        # step inputs in one device buffer (one host-to-device copy per step):
+        # tokens | positions | slots | ctx | tables [B, max_blocks]
+        self.inputs = torch.zeros(4 * B + B * max_blocks_per_seq, **i32)
+        self.tokens, self.positions, self.slots, self.ctx = (self.inputs[i * B:(i + 1) * B] for i in range(4))
+        self.ctx.fill_(1)
+        self.tables = self.inputs[4 * B:].view(B, max_blocks_per_seq)
         self.next_tokens = torch.zeros(B, **i32)
         self.h = torch.zeros((B, H), dtype=torch.float32, device=dev)
         self.x = torch.zeros((B, H), dtype=torch.bfloat16, device=dev)
@@ -264,6 +266,7 @@ class DecodeEngine:
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
         # pinned host staging for step inputs: tokens, positions, slots, ctx, then the table
         self.stage = torch.zeros(4 * B + B * max_blocks_per_seq, dtype=torch.int32, pin_memory=True)
+        self.stage_np = self.stage.numpy()
         self.graphs: dict = {}
         # TP > 1: row-parallel linears push their partials straight into every rank's memory and a
         # fused reduce(+norm) kernel finishes the all-reduce (MG_FUSED_AR=0 falls back to NCCL).
@@ -356,27 +359,29 @@ class DecodeEngine:
                 K.argmax_rows(self.logits[:b], out=self.next_tokens[:b])
 
     def set_inputs(self, tokens, positions, slots, ctx, tables) -> int:
-        """Stage one step's inputs in pinned host memory and copy them to the static device
-        buffers (async on the current stream). Returns the batch size; also records the
+        """Stage one step's inputs in pinned host memory and copy them to the device input buffer in
+        one asynchronous copy on the current stream. Returns the batch size; also records the
         host-to-device bytes of the step in ``self.h2d_bytes``."""
         b = len(tokens)
         if b > self.max_batch:
             raise ValueError(f"batch {b} > max_batch {self.max_batch}")
-        t = torch.as_tensor(tables, dtype=torch.int32)
+        t = np.asarray(tables, dtype=np.int32)
+        if t.ndim != 2 or t.shape[0] != b:
+            raise ValueError("tables must be [batch, blocks]")
         w = t.shape[1]
         if w > self.max_blocks:
             raise ValueError(f"block table of {w} blocks > {self.max_blocks}")
         torch.cuda.current_stream(self.device).synchronize()  # the staging buffer may still be in flight
-        st = self.stage
-        B = self.max_batch
+        st = self.stage_np
+        B, MB = self.max_batch, self.max_blocks
         for i, v in enumerate((tokens, positions, slots, ctx)):
-            st[i * B:i * B + b] = torch.as_tensor(v, dtype=torch.int32)
-        tab = st[4 * B:4 * B + b * w].view(b, w)
-        tab.copy_(t)
-        for i, dst in enumerate((self.tokens, self.positions, self.slots, self.ctx)):
-            dst[:b].copy_(st[i * B:i * B + b], non_blocking=True)
-        self.tables[:b, :w].copy_(tab, non_blocking=True)
-        self.h2d_bytes = 4 * (4 * b + b * w)
+            st[i * B:i * B + b] = v
+        tab = st[4 * B:4 * B + b * MB].reshape(b, MB)
+        tab[:, :w] = t
+        tab[:, w:] = 0
+        n = 4 * B + b * MB
+        self.inputs[:n].copy_(self.stage[:n], non_blocking=True)
+        self.h2d_bytes = 4 * n
         return b
 
     # ---- CUDA graphs -------------------------------------------------------------------------------
