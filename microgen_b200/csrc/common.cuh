@@ -46,6 +46,16 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 
 bool mg_pdl_enabled();
 
+// True the first time it is called for `flags` on the current device (function attributes such as
+// the dynamic shared-memory limit belong to the current device's copy of the kernel).
+inline bool mg_first_on_device(bool (&flags)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
+  if (flags[dev]) return false;
+  flags[dev] = true;
+  return true;
+}
+
 // Host: a 2-D tiled TMA descriptor (row-major [outer][inner], row_bytes apart; box_inner x box_outer).
 int mg_make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);

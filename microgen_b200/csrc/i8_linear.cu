@@ -564,11 +564,9 @@ int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
               const float* bias, int64_t n, void* y, int64_t ldy, int epi, int split, cudaStream_t st,
               bool packed, const PeerOut* po) {
   using C = TcCfg<MP>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static bool attr_done[64] = {};
+  if (mg_first_on_device(attr_done))
     MG_CUDA_TRY(cudaFuncSetAttribute(i8_gemm_tc<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    attr_done = true;
-  }
   CUtensorMap mw, mx;
   const uint64_t packed_rows = (uint64_t)((n + kBN - 1) / kBN) * ((k + kBK - 1) / kBK) * kBN;
   int rc = packed ? make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, kBK, packed_rows, kBK, kBK, kBN)

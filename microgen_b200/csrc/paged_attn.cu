@@ -560,13 +560,12 @@ Plan make_plan(int b, int hq, int hkv, int d, int max_blocks, int n_shared) {
 template <int D>
 int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v_pool, cudaStream_t st) {
   using C = AttnCfg<D>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static bool attr_done[64] = {};
+  if (mg_first_on_device(attr_done)) {
     MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::kSmem));
     MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::kSmem));
-    attr_done = true;
   }
   // Pools as 2-D tensors [num_blocks*hkv*16 rows, D]: rows of one (block, kv head) tile are adjacent.
   const uint64_t rows = (uint64_t)p.num_blocks * p.hkv * 16;
