@@ -1,4 +1,4 @@
-"""Tensor-parallel host logic on CPU with world-size-2 ``gloo`` process groups (no GPU).
+"""Tensor-parallel host logic on CPU with world-size-2 and -4 ``gloo`` process groups (no GPU).
 
 * the row-parallel reduction protocol (``row_parallel_residual``): rank 0 adds its partial into the
   residual, the others store theirs, one sum all-reduce — must equal ``h + Σ partials + bias``, the
@@ -58,8 +58,9 @@ def _protocol_worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def test_row_parallel_residual_protocol_world2():
-    for r in _run(_protocol_worker, 2):
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_parallel_residual_protocol(world):
+    for r in _run(_protocol_worker, world):
         torch.testing.assert_close(r["h"], r["want"], rtol=1e-6, atol=1e-6)
 
 
@@ -69,11 +70,17 @@ def _oracle_quantize(w: torch.Tensor):
     return torch.from_numpy(q), torch.from_numpy(s)
 
 
-def _load(rank, world):
+def _shape(world):
+    from tests._hf_models import TINY
+    # world 4 needs 4 | kv heads and 64-row gate/up groups per rank: 8/4 heads, inter 256
+    return dict(TINY["llama"]) if world <= 2 else dict(TINY["llama"], heads=8, kv_heads=4)
+
+
+def _load(rank, world, shape):
     from microgen_b200.engine import WeightLoader
     from microgen_b200.model_spec import spec_from_hf_config
-    from tests._hf_models import TINY, make_hf_model
-    model, _ = make_hf_model(TINY["llama"], seed=0)
+    from tests._hf_models import make_hf_model
+    model, _ = make_hf_model(shape, seed=0)
     spec = spec_from_hf_config(model.config)
     state = {k: v.detach() for k, v in model.state_dict().items()}
     w = WeightLoader(spec, "cpu", rank, world, pack=False, quantize=_oracle_quantize).load(state)
@@ -82,7 +89,7 @@ def _load(rank, world):
 
 def _shard_worker(rank, world, port, outdir):
     _init(rank, world, port)
-    spec, w = _load(rank, world)
+    spec, w = _load(rank, world, _shape(world))
     L = w.layers[0]
     torch.save({"qkv_q": L.qkv_q, "qkv_s": L.qkv_s, "o_q": L.o_q, "o_s": L.o_s, "gu_q": L.gu_q, "gu_s": L.gu_s,
                 "d_q": L.d_q, "d_s": L.d_s, "lm_q": w.lm_q}, os.path.join(outdir, f"r{rank}.pt"))
@@ -96,14 +103,15 @@ def _deinterleave(q):
     return g[:, 0].reshape(-1, *q.shape[1:]), g[:, 1].reshape(-1, *q.shape[1:])
 
 
-def test_tp2_shards_reassemble_tp1_codes():
-    spec, full = _load(0, 1)
-    shards = _run(_shard_worker, 2)
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_shards_reassemble_tp1_codes(world):
+    spec, full = _load(0, 1, _shape(world))
+    shards = _run(_shard_worker, world)
     D, hq, hkv = spec.head_dim, spec.heads, spec.kv_heads
     F = full.layers[0]
     qn, kn = hq * D, hkv * D
-    # column-parallel q/k/v: each rank holds hq/2 query heads then hkv/2 k heads then hkv/2 v heads
-    per_q, per_k = qn // 2, kn // 2
+    # column-parallel q/k/v: each rank holds hq/W query heads then hkv/W k heads then hkv/W v heads
+    per_q, per_k = qn // world, kn // world
     for part, (a, n) in enumerate([(0, qn), (qn, kn), (qn + kn, kn)]):
         per = per_q if part == 0 else per_k
         off = 0 if part == 0 else (per_q if part == 1 else per_q + per_k)
