@@ -271,7 +271,9 @@ class DecodeEngine:
         # TP > 1: row-parallel linears push their partials straight into every rank's memory and a
         # fused reduce(+norm) kernel finishes the all-reduce (MG_FUSED_AR=0 falls back to NCCL).
         self.comm = None
-        if world > 1 and os.environ.get("MG_FUSED_AR", "1") != "0" and isinstance(weights.lm_q, K.PackedWeight):
+        # (the push epilogue works on whole 128-row output tiles: hidden % 128 == 0, else NCCL)
+        if (world > 1 and os.environ.get("MG_FUSED_AR", "1") != "0" and isinstance(weights.lm_q, K.PackedWeight)
+                and spec.hidden % 128 == 0 and spec.hidden <= 8192):
             self.comm = K.Comm(rank, world, max_batch * spec.hidden, group=group)
 
     # ---- the step -----------------------------------------------------------------------------
