@@ -51,3 +51,25 @@ def test_non_compute_entry_points(lib):
     assert L.mg_i8_linear(None, 1, 15, 16, None, None, None, 8, None, 8, 0, None) == _lib.MG_ERR_INVALID_ARG
     out = ctypes.c_size_t(123)
     assert L.mg_paged_attn_workspace_bytes(4, 24, 8, 96, 10, 0, ctypes.byref(out)) == _lib.MG_ERR_UNSUPPORTED
+
+
+def test_argument_errors_of_later_entry_points(lib):
+    """Bad arguments come back as MG_ERR_INVALID_ARG before any CUDA call (no GPU needed)."""
+    from microgen_b200 import _lib
+    L = _lib.load()
+    bad = _lib.MG_ERR_INVALID_ARG
+    h = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(L.mg_comm_handle_bytes())
+    assert L.mg_comm_handle_bytes() > 0
+    assert L.mg_comm_create(0, 0, 16, ctypes.byref(h), handle) == bad          # world < 1
+    assert L.mg_comm_create(2, 2, 16, ctypes.byref(h), handle) == bad          # rank >= world
+    assert L.mg_comm_create(0, 9, 16, ctypes.byref(h), handle) == bad          # world > 8
+    assert L.mg_comm_open(None, handle) == bad
+    assert L.mg_comm_destroy(None) == bad
+    assert L.mg_i8_linear_packed_rowpar(None, 1, 128, 128, None, None, 128, None, 0, None) == bad
+    assert L.mg_rowpar_reduce_norm(None, None, None, 1, 128, 1, None, None, ctypes.c_float(1e-5), None,
+                                   None) == bad
+    assert L.mg_argmax_rows(None, 1, 8, 8, None, None) == bad
+    assert L.mg_argmax_rows(None, 1, 8, 4, None, None) == bad                   # ld < n
+    assert L.mg_paged_decode_attn(None, None, None, 1, None, 1, None, 1, 24, 7, 128, 0, ctypes.c_float(1.0),
+                                  None, None, 0, None) == bad                   # hq % hkv != 0
