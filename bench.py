@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload llama3b|qwen05b|gpt2]
     python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...   (N > 1, TP = N)
     python bench.py --impl reference ...   (the reference's CPU path, restated as the oracle port)
+    python bench.py --sweep c4 [--steps R]  (isolated kernel sweep; torchrun for the sharded cases)
 
 Workload (default): Llama-3.2-3B-shaped decoder (28 layers, hidden 3072, 24/8 heads of 128,
 SwiGLU 8192, vocab 128256), random-init N(0, 0.02) weights quantized to INT8 per output
@@ -49,6 +50,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (debug)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
+    ap.add_argument("--sweep", default="", choices=["", "c4"],
+                    help="c4: the isolated INT8-linear and paged-attention kernel sweep, one JSON line per case")
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: KV filled with random values instead of a prefill, no window centering, "
                          "no probe / e2e / CPU legs")
@@ -162,6 +165,163 @@ def push_chain(eng, spec, b: int, reps: int = 10) -> dict:
             "nominal_gbs": 900.0, "frac": round(egress / us / 1e3 / 770.0, 4),
             "timing": f"CUDA graph of the step's {n_ar} row-parallel push linears + reduce kernels, {reps} "
                       "replays, CUDA events, max over ranks (linear compute included)"}
+
+
+C4_LINEAR = [(3072, 9216), (3072, 8192), (8192, 3072), (4096, 14336)]  # (K, N)
+C4_M = [1, 8, 32, 128, 256]
+C4_ATTN = dict(hq=32, hkv=8, d=128, ctx=[512, 2048, 8192, 32768], batch=[1, 16, 64])
+
+
+def _timed(fn, reps: int, flush) -> float:
+    """Mean device microseconds of ``fn()``: each launch follows an L2 flush (a read of a buffer larger
+    than L2) and sits between two CUDA events on the launch stream; ``fn`` must do no host synchronisation."""
+    import torch
+    st = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    fn()
+    torch.cuda.synchronize()
+    for a, b in evs:
+        flush.sum()  # read (not write) the buffer: L2 is left holding clean lines of it
+        a.record(st)
+        fn()
+        b.record(st)
+    torch.cuda.synchronize()
+    return 1e3 * sum(a.elapsed_time(b) for a, b in evs) / reps
+
+
+def sweep_c4(args) -> None:
+    """Isolated kernel sweep (one JSON line per configuration):
+
+    * INT8 linear, (K, N) x M: W N(0, 0.02) quantized per output channel on the device, x bf16 N(0, 1).
+      At N GPUs (torchrun) each rank runs its column-parallel shard (N/world output rows) and its
+      row-parallel shard (K/world input columns) with the fused peer-memory all-reduce (push + reduce),
+      and the same row-parallel partial followed by an NCCL all_reduce (the baseline), max over ranks.
+      At one GPU the column and row shards are the whole matrix; the tensor-core kernel (tile-packed codes)
+      and the CUDA-core GEMV (row-major codes) are both timed.
+    * Paged decode attention: 32 query / 8 KV heads, head_dim 128, bf16 K/V N(0, 1), shuffled block tables,
+      the first half of each sequence's blocks shared by the batch (read once per batch).
+    Algorithmic bytes: linear K*N codes + 4N scales + 2MK x + 2MN y; attention the unique K/V bytes + q + out."""
+    import torch
+    import torch.distributed as dist
+    from microgen_b200 import kernels as K
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    hbm, hbm_kind = peaks()
+    flush = torch.ones(80 << 20, dtype=torch.float32, device=dev)  # 320 MB
+    reps = max(3, args.steps)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def emit(d):
+        if rank == 0:
+            print(json.dumps(d), flush=True)
+
+    def maxrank(us):
+        if world == 1:
+            return us
+        t = torch.tensor([us], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    comm = None
+    if world > 1:
+        comm = K.Comm(rank, world, max(C4_M) * max(n for _, n in C4_LINEAR))
+    for k, n in C4_LINEAR:
+        w = torch.randn((n, k), generator=g, device=dev).mul_(0.02)
+        q, s = K.quantize_rows_i8(w)
+        del w
+        qp = K.pack_weights(q)
+        ncol, krow = n // world, k // world
+        qc = K.pack_weights(q[rank * ncol:(rank + 1) * ncol].contiguous()) if world > 1 else qp
+        sc = s[rank * ncol:(rank + 1) * ncol].contiguous() if world > 1 else s
+        qr_rm = q[:, rank * krow:(rank + 1) * krow].contiguous() if world > 1 else q
+        qr = K.pack_weights(qr_rm) if world > 1 else qp
+        for m in C4_M:
+            x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            line = {"sweep": "c4_linear", "K": k, "N": n, "M": m, "world": world,
+                    "bytes": k * n + 4 * n + 2 * m * k + 2 * m * n, "peak_gbs": hbm, "peak_source": hbm_kind,
+                    "l2": "flushed before every launch"}
+            if world == 1:
+                us_tc = _timed(lambda: K.i8_linear(x, qp, s, y=y, epilogue=K.EPI_STORE_BF16), reps, flush)
+                us_simt = _timed(lambda: K.i8_linear(x, q, s, y=y, epilogue=K.EPI_STORE_BF16, algo="simt"), reps,
+                                 flush)
+                for name, us in (("tc", us_tc), ("simt", us_simt)):
+                    gbs = line["bytes"] / us / 1e3
+                    line[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4)}
+            else:
+                xc = x
+                yc = torch.empty((m, ncol), dtype=torch.bfloat16, device=dev)
+                us_col = maxrank(_timed(lambda: K.i8_linear(xc, qc, sc, y=yc, epilogue=K.EPI_STORE_BF16), reps,
+                                        flush))
+                xr = x[:, rank * krow:(rank + 1) * krow]
+                h = torch.zeros((m, n), dtype=torch.float32, device=dev)
+
+                def fused():
+                    K.i8_linear_rowpar(xr, qr, s, comm)
+                    K.rowpar_reduce_norm(comm, h, None, K.NORM_NONE)
+
+                def nccl():
+                    K.i8_linear(xr, qr, s, y=h, epilogue=K.EPI_STORE_F32)
+                    dist.all_reduce(h)
+
+                dist.barrier()
+                us_fused = maxrank(_timed(fused, reps, flush)) if n % 128 == 0 and n <= 8192 else None
+                dist.barrier()
+                us_nccl = maxrank(_timed(nccl, reps, flush))
+                col_bytes = k * ncol + 4 * ncol + 2 * m * k + 2 * m * ncol
+                row_bytes = krow * n + 4 * n + 2 * m * krow + 4 * m * n
+                line.update({"column": {"us": round(us_col, 2), "gbs_per_rank": round(col_bytes / us_col / 1e3, 1)},
+                             "row_fused": None if us_fused is None else
+                             {"us": round(us_fused, 2), "gbs_per_rank": round(row_bytes / us_fused / 1e3, 1),
+                              "nvlink_egress_bytes": (world - 1) * m * n * 4},
+                             "row_nccl": {"us": round(us_nccl, 2), "gbs_per_rank": round(row_bytes / us_nccl / 1e3, 1)},
+                             "timing": "max over ranks of per-rank CUDA-event means"})
+            emit(line)
+        del q, qp, qc, qr, qr_rm
+    if comm is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+    # ---- attention (every rank runs the same single-GPU cases; rank 0 reports)
+    import random
+    hq, hkv, d = C4_ATTN["hq"], C4_ATTN["hkv"], C4_ATTN["d"]
+    for ctx in C4_ATTN["ctx"]:
+        for b in C4_ATTN["batch"]:
+            nb = (ctx + 15) // 16
+            ns = nb // 2
+            nblocks = ns + b * (nb - ns)
+            order = list(range(nblocks))
+            random.Random(ctx * 131 + b).shuffle(order)
+            tables = torch.empty((b, nb), dtype=torch.int32)
+            tables[:, :ns] = torch.tensor(order[:ns], dtype=torch.int32)
+            for i in range(b):
+                tables[i, ns:] = torch.tensor(order[ns + i * (nb - ns):ns + (i + 1) * (nb - ns)], dtype=torch.int32)
+            kp = torch.randn((nblocks, hkv, 16, d), generator=g, device=dev).to(torch.bfloat16)
+            vp = torch.randn((nblocks, hkv, 16, d), generator=g, device=dev).to(torch.bfloat16)
+            qq = torch.randn((b, hq, d), generator=g, device=dev)
+            tab = tables.to(dev)
+            ctxs = torch.full((b,), ctx, dtype=torch.int32, device=dev)
+            out = torch.empty((b, hq * d), dtype=torch.bfloat16, device=dev)
+            ws = torch.empty(max(16, K.attn_workspace_bytes(b, hq, hkv, d, nb, ns)), dtype=torch.uint8, device=dev)
+            us = _timed(lambda: K.paged_decode_attn(qq, kp, vp, tab, ctxs, d ** -0.5, n_shared_blocks=ns, out=out,
+                                                    workspace=ws, validate=False), reps, flush)
+            nbytes = (ns * 16 + b * (ctx - ns * 16)) * hkv * d * 2 * 2 + b * hq * d * (4 + 2)
+            gbs = nbytes / us / 1e3
+            emit({"sweep": "c4_attention", "ctx": ctx, "batch": b, "hq": hq, "hkv": hkv, "d": d,
+                  "shared_blocks": ns, "bytes": nbytes, "us": round(us, 2), "gbs": round(gbs, 1),
+                  "frac": round(gbs / hbm, 4), "peak_gbs": hbm, "peak_source": hbm_kind,
+                  "l2": "flushed before every launch"})
+            del kp, vp
+    K.check_device()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def peaks() -> tuple[float, str]:
@@ -291,6 +451,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.sweep == "c4":
+        sweep_c4(args)
         return
     import torch
     import torch.distributed as dist

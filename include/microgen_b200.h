@@ -61,8 +61,8 @@ int mg_quantize_rows_i8(const float* w, int64_t n, int64_t k, int8_t* q, float* 
 /* ---- INT8 weight-only linear (quantized.py:24-27; parallel.py shards) ---------------------- */
 /* y = epilogue( x[m,k] (bf16, row stride ldx) · (q[n,k]·scales[n])ᵀ + bias[n] ), fp32 accumulate.
  * bias is fp32 [n] or NULL. k % 16 == 0, ldx % 8 == 0, 16-byte aligned x and q.
- * mg_i8_linear picks the kernel: the tcgen05 tensor-core kernel for every m, unless
- * MG_EPI_SWIGLU needs n % 128 == 0 and it does not hold. */
+ * mg_i8_linear runs the tcgen05 tensor-core kernel on row-major codes for every m; MG_EPI_SWIGLU
+ * needs n % 128 == 0 (whole 64-row gate/up pairs), otherwise the call returns MG_ERR_INVALID_ARG. */
 int mg_i8_linear(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q, const float* scales,
                  const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, void* stream);
 /* Same contract, CUDA-core kernel (one warp per output row, 128-bit weight loads). */
@@ -90,8 +90,9 @@ int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t ldx, const 
  *   mg_comm_destroy unmaps and frees.
  * mg_i8_linear_packed_rowpar runs this rank's partial of a row-parallel linear (tile-packed codes, scale
  * applied, no bias) and its epilogue stores each output tile straight into every rank's receive slot over
- * NVLink as words {two bf16 values, all-reduce epoch} (n % 128 == 0). mg_rowpar_reduce_norm waits (at most about 1 s, then
- * MG_ERR_TIMEOUT in the device error word) until every word it sums carries the current epoch, sets
+ * NVLink as words {two bf16 values, all-reduce epoch} (n % 128 == 0). mg_rowpar_reduce_norm waits (at most
+ * MG_PEER_TIMEOUT_MS from the environment of mg_comm_create, default 1000 ms; then MG_ERR_TIMEOUT in the
+ * device error word) until every word it sums carries the current epoch, sets
  * h += sum over ranks (rank order) +
  * bias, and with norm = 1 (RMSNorm, w) or 2 (LayerNorm, w, wb) writes x = bf16(norm(h)). Every rank must
  * issue the same sequence of rowpar / reduce calls. m * n <= slot_elems. */
@@ -136,9 +137,12 @@ int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool,
  * Limit: returns MG_ERR_UNSUPPORTED when mg_paged_attn_workspace_bytes() for the sizes exceeds the array.
  * Allocates nothing (no cudaMalloc / cudaFree / allocating library call). The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress, once per device, with that device current);
- * make that first call before any stream capture. All calls share the array: calls whose kernels
- * overlap on the GPU (e.g. on two streams) race on it — serialise them. Nothing in it needs clearing:
- * each call writes every slot it later reads. */
+ * make that first call before any stream capture. The address is kept for the life of the process:
+ * after cudaDeviceReset (which unloads the library's device code) this entry point must not be called
+ * again on that device. All calls share the array: calls whose kernels overlap on the GPU (e.g. on two
+ * streams) race on it — serialise them. Nothing in it needs clearing: each call writes every slot it
+ * later reads (a split whose bounded wait gave up writes an empty softmax state and records
+ * MG_ERR_TIMEOUT). */
 #define MG_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
 int mg_paged_decode_attn_noalloc(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
                                  const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,

@@ -15,6 +15,8 @@ Prefill runs the prompt through the decode kernels one position at a time (all
 sequences of the batch per launch). Prompts that share a leading run of whole
 16-token blocks are prefilled once for that prefix (batch 1) and the blocks are
 shared by reference count; the attention kernel then reads them once per batch.
+With ``prefix_cache_capacity`` > 0 such prefixes are also kept across calls
+(``runtime/prefix_cache.py``, the paged form of the reference's ``PrefixKVCache``).
 
 ``B200TensorParallelBackend`` is SPMD: one process per GPU, every rank making the
 same calls in the same order; logits are identical on every rank.
@@ -30,7 +32,8 @@ import torch.nn as nn
 from .. import kernels as K
 from ..engine import DecodeEngine, WeightLoader
 from ..model_spec import spec_from_hf_config
-from ..runtime.paged_kv import BlockTable, PagedKVCacheAllocator, TableMirror
+from ..runtime.paged_kv import BlockTable, PagedKVCacheAllocator, TableMirror, check_shared_prefix
+from ..runtime.prefix_cache import PagedPrefixCache
 
 BLOCK = 16
 
@@ -65,6 +68,7 @@ class PagedKVCache:
         self.prefix: Optional[BlockTable] = None
         self.n_shared_blocks = 0
         self.mirror: Optional[TableMirror] = None  # host copy of the block tables for decode steps
+        self.reused_prefix_tokens = 0  # prompt tokens whose K/V came from the backend's prefix cache
 
     def __bool__(self) -> bool:
         return True
@@ -95,7 +99,16 @@ class B200QuantizedBackend:
 
     def __init__(self, device=None, quant_type: str = "int8", max_batch: int = 64, max_seq_len: int = 4096,
                  num_blocks: Optional[int] = None, use_cuda_graph: bool = True, free_list_seed: Optional[int] = None,
-                 world_size: int = 1, group=None) -> None:
+                 world_size: int = 1, group=None, device_check_every: int = 1,
+                 prefix_cache_capacity: int = 0) -> None:
+        """``device_check_every``: after every that many ``decode`` calls, read the library's device error
+        word (one stream synchronisation) and raise — TimeoutError when a bounded wait gave up (a peer
+        rank that never pushed its row-parallel partial), RuntimeError for a failed device-side check —
+        instead of returning logits computed from incomplete data. 0 turns the check off.
+
+        ``prefix_cache_capacity`` > 0 keeps a block-level prefix cache (``PagedPrefixCache``) of that many
+        entries: a prefill whose prompts start with a cached run of whole blocks shares those blocks instead
+        of recomputing them, and every prefill's whole-block common prefix is cached for later calls."""
         if quant_type.lower() != "int8":
             raise ValueError("the B200 decode path implements INT8 per-channel weights only")
         if isinstance(device, CUDADeviceInfo):
@@ -109,6 +122,10 @@ class B200QuantizedBackend:
         self.use_cuda_graph = use_cuda_graph
         self.free_list_seed = free_list_seed
         self.world_size, self.group = world_size, group
+        self.device_check_every = max(0, int(device_check_every))
+        self._decodes = 0
+        self.prefix_cache_capacity = int(prefix_cache_capacity)
+        self.prefix_cache: Optional[PagedPrefixCache] = None
         self.rank = torch.distributed.get_rank(group) if world_size > 1 else 0
         self.engine: Optional[DecodeEngine] = None
         self.allocator: Optional[PagedKVCacheAllocator] = None
@@ -140,6 +157,8 @@ class B200QuantizedBackend:
         self.allocator = PagedKVCacheAllocator(num_blocks=self.num_blocks, block_size=BLOCK)
         if self.free_list_seed is not None:
             self.allocator.shuffle_free_list(self.free_list_seed)
+        if self.prefix_cache_capacity > 0:
+            self.prefix_cache = PagedPrefixCache(self.allocator, self.prefix_cache_capacity)
         self.spec = spec
         self._quantized = True
 
@@ -167,6 +186,7 @@ class B200QuantizedBackend:
         if cache_mirror is None:
             cache_mirror = TableMirror(b, eng.max_blocks)
         tab = cache_mirror.update(tables)
+        check_shared_prefix(tab, n_shared)
         eng.set_inputs(tokens, positions, slots, ctx, tab)
         if self.use_cuda_graph:
             eng.capture(b, n_shared, compute_logits=logits).replay()
@@ -190,18 +210,31 @@ class B200QuantizedBackend:
                 lcp = T
                 for row in ids[1:]:
                     lcp = min(lcp, next((i for i, (a, c) in enumerate(zip(ids[0], row)) if a != c), T))
-                n_shared = min(lcp, T - 1) // BLOCK if b > 1 else 0
-                if n_shared:
-                    cache.prefix = self.allocator.allocate_sequence("prefix", n_shared * BLOCK)
+                n_prefix = min(lcp, T - 1) // BLOCK
+                if not (b > 1 or self.prefix_cache is not None):
+                    n_prefix = 0
+                if n_prefix:
+                    # the prefix's blocks: those a cached prefix already holds, then computed ones (batch 1)
+                    toks = ids[0][:n_prefix * BLOCK]
+                    hit = self.prefix_cache.match_prefix(toks) if self.prefix_cache is not None else None
+                    reused = hit[0] // BLOCK if hit is not None else 0
+                    if reused:
+                        cache.prefix = self.allocator.share_prefix(hit[1], reused, "prefix", n_prefix * BLOCK)
+                    else:
+                        cache.prefix = self.allocator.allocate_sequence("prefix", n_prefix * BLOCK)
                     prefix_mirror = TableMirror(1, eng.max_blocks)
-                    for p in range(n_shared * BLOCK):
+                    for p in range(reused * BLOCK, n_prefix * BLOCK):
                         self._run([cache.prefix], [ids[0][p]], [p], 0, logits=False, cache_mirror=prefix_mirror)
-                    cache.tables = [self.allocator.share_prefix(cache.prefix, n_shared, f"seq{i}", T)
+                    if self.prefix_cache is not None:
+                        self.prefix_cache.insert(toks, cache.prefix)
+                    cache.tables = [self.allocator.share_prefix(cache.prefix, n_prefix, f"seq{i}", T)
                                     for i in range(b)]
-                    start = n_shared * BLOCK
+                    cache.reused_prefix_tokens = reused * BLOCK
+                    start = n_prefix * BLOCK
                 else:
                     cache.tables = [self.allocator.allocate_sequence(f"seq{i}", T) for i in range(b)]
-                cache.n_shared_blocks = n_shared
+                # the attention kernel's shared-prefix CTAs serve a batch; one sequence reads its blocks itself
+                cache.n_shared_blocks = n_prefix if b > 1 else 0
             else:
                 if len(cache.tables) != b:
                     raise ValueError("cache holds a different batch size")
@@ -235,6 +268,9 @@ class B200QuantizedBackend:
             if cache.mirror is None or cache.mirror.arr.shape[0] < b:
                 cache.mirror = TableMirror(b, eng.max_blocks)
             self._run(cache.tables, toks, positions, cache.n_shared_blocks, logits=True, cache_mirror=cache.mirror)
+            self._decodes += 1
+            if self.device_check_every and self._decodes % self.device_check_every == 0:
+                K.check_device()
             return eng.logits[:b].clone(), cache
 
     def sample(self, logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0,

@@ -1,4 +1,5 @@
-"""Tensor-parallel INT8 linears (mirror of ``microgen/backends/parallel.py:12-81``).
+"""Tensor-parallel INT8 linears (mirror of ``microgen/backends/parallel.py:12-81``) and the module walk
+that installs them (``parallel.py:108-131``).
 
 Split rules follow the reference: out-features (column) or in-features (row) split in
 ``N // world`` slices, the last rank taking the remainder; the row-parallel bias is
@@ -114,3 +115,36 @@ class RowParallelLinear(_TPBase):
         if self.bias is not None:
             y = y + self.bias
         return y.to(x.dtype).reshape(*shape[:-1], y.shape[-1])
+
+
+# Child-name patterns of the reference's TP walk (``parallel.py:113-128``): column-parallel projections,
+# then row-parallel ones. ``lm_head`` matches neither and stays as it is (the reference leaves it unsharded).
+COLUMN_NAMES = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "fc1", "c_attn")
+ROW_NAMES = ("o_proj", "down_proj", "fc2", "c_proj")
+
+
+def apply_tensor_parallelism(model: nn.Module, world_size: int, group=None, device=None) -> nn.Module:
+    """Install INT8 ``ColumnParallelLinear`` / ``RowParallelLinear`` modules in place of ``model``'s
+    ``nn.Linear`` children, classified by child name as the reference's
+    ``TensorParallelPyTorchBackend.apply_tensor_parallelism`` does (``parallel.py:108-131``): a name containing
+    one of ``COLUMN_NAMES`` becomes column-parallel, else one containing one of ``ROW_NAMES`` becomes
+    row-parallel, others are left alone; non-Linear children are walked recursively. Each replacement
+    quantizes the FULL weight and keeps its shards (all of them with ``group=None``, this rank's with a
+    process group). Returns ``model``."""
+    if world_size < 1:
+        raise ValueError("world_size must be >= 1")
+
+    def walk(module: nn.Module) -> None:
+        for name, child in list(module.named_children()):
+            if isinstance(child, nn.Linear):
+                low = name.lower()
+                bias = child.bias.data if child.bias is not None else None
+                if any(p in low for p in COLUMN_NAMES):
+                    setattr(module, name, ColumnParallelLinear(child.weight.data, bias, world_size, group, device))
+                elif any(p in low for p in ROW_NAMES):
+                    setattr(module, name, RowParallelLinear(child.weight.data, bias, world_size, group, device))
+            else:
+                walk(child)
+
+    walk(model)
+    return model

@@ -73,11 +73,14 @@ extern "C" int mg_device_error(void* stream, int clear, int* code, int* info) {
   cudaStream_t s = mg_stream(stream);
   int vals[2] = {0, 0};
   MG_CUDA_TRY(cudaMemcpyFromSymbolAsync(&vals[0], g_mg_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
-  MG_CUDA_TRY(cudaMemcpyFromSymbolAsync(&vals[1], g_mg_dev_error_info, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
   MG_CUDA_TRY(cudaStreamSynchronize(s));
+  if (vals[0] != MG_OK) {  // the common case (no error) costs one read and one synchronisation
+    MG_CUDA_TRY(cudaMemcpyFromSymbolAsync(&vals[1], g_mg_dev_error_info, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
+    MG_CUDA_TRY(cudaStreamSynchronize(s));
+  }
   *code = vals[0];
   if (info) *info = vals[1];
-  if (clear) {
+  if (clear && vals[0] != MG_OK) {
     const int zero[2] = {0, 0};
     MG_CUDA_TRY(cudaMemcpyToSymbolAsync(g_mg_dev_error, &zero[0], sizeof(int), 0, cudaMemcpyHostToDevice, s));
     MG_CUDA_TRY(cudaMemcpyToSymbolAsync(g_mg_dev_error_info, &zero[1], sizeof(int), 0, cudaMemcpyHostToDevice, s));

@@ -13,6 +13,7 @@
 //
 // Reuse of a set is safe without extra handshakes: a rank pushes e+2 only after its reduce e+1 saw
 // every peer's words of e+1, and a peer pushes e+1 only after its own reduce e consumed set e%2.
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -21,11 +22,15 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxV = 8;                     // float4 per thread: rows up to 8192
-constexpr uint64_t kWaitNs = 1000000000ull;  // a peer that has not pushed within 1 s is reported
+// A peer that has not pushed within the communicator's limit is reported: MG_PEER_TIMEOUT_MS in the
+// environment of mg_comm_create (default 1000 ms; ranks whose host sides drift apart by more than that,
+// e.g. through uneven start-up work, need a larger value).
+constexpr uint64_t kDefaultWaitNs = 1000000000ull;
 
 struct Comm {
   int rank = 0, world = 1, device = 0;
   int64_t slot = 0;
+  uint64_t timeout_ns = kDefaultWaitNs;
   size_t recv_bytes = 0, bytes = 0;
   char* base = nullptr;
   cudaIpcMemHandle_t handle{};
@@ -50,9 +55,9 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // Waits until the two words at p (four values, 16-byte aligned) carry `epoch`. Gives up once `dead`
-// is set or the wait has run for kWaitNs, recording MG_ERR_TIMEOUT with the peer rank in the detail.
+// is set or the wait has run for limit_ns, recording MG_ERR_TIMEOUT with the peer rank in the detail.
 __device__ __forceinline__ void wait_words(const uint64_t* p, uint32_t epoch, uint64_t (&wd)[2], uint64_t& t0,
-                                           bool& dead, int r) {
+                                           bool& dead, int r, uint64_t limit_ns) {
   for (uint32_t spin = 0;; ++spin) {
     ld_volatile_v2u64(p, wd[0], wd[1]);
     if (dead || ((uint32_t)(wd[0] >> 32) == epoch && (uint32_t)(wd[1] >> 32) == epoch)) return;
@@ -60,7 +65,7 @@ __device__ __forceinline__ void wait_words(const uint64_t* p, uint32_t epoch, ui
       const uint64_t t = global_ns();
       if (t0 == 0) {
         t0 = t;
-      } else if (t - t0 > kWaitNs) {
+      } else if (t - t0 > limit_ns) {
         mg_record_error(MG_ERR_TIMEOUT, 600 + r);
         dead = true;
         return;
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
       float4 a = reinterpret_cast<const float4*>(hr)[idx];
       for (int r = 0; r < po.world; ++r) {
         uint64_t wd[2];
-        wait_words(recv + (int64_t)r * po.slot + idx * 2, epoch, wd, t0, dead, r);
+        wait_words(recv + (int64_t)r * po.slot + idx * 2, epoch, wd, t0, dead, r, po.timeout_ns);
         a.x += bf16lo((uint32_t)wd[0]);
         a.y += bf16hi((uint32_t)wd[0]);
         a.z += bf16lo((uint32_t)wd[1]);
@@ -162,6 +167,7 @@ int mg_comm_peer_out(void* comm, PeerOut* out) {
   po.count = reinterpret_cast<uint32_t*>(c->base + c->recv_bytes);
   po.done = po.count + 1;
   po.slot = c->slot;
+  po.timeout_ns = c->timeout_ns;
   po.rank = c->rank;
   po.world = c->world;
   *out = po;
@@ -177,6 +183,10 @@ extern "C" int mg_comm_create(int rank, int world, int64_t slot_elems, void** co
   c->rank = rank;
   c->world = world;
   c->slot = ((slot_elems + 1) / 2 + 63) / 64 * 64;  // words of two values
+  if (const char* v = getenv("MG_PEER_TIMEOUT_MS")) {
+    const long long ms = atoll(v);
+    if (ms > 0) c->timeout_ns = (uint64_t)ms * 1000000ull;
+  }
   c->recv_bytes = align_up((size_t)2 * world * c->slot * sizeof(uint64_t), 256);
   c->bytes = c->recv_bytes + 256;  // + the two local counters
   cudaError_t e = cudaGetDevice(&c->device);

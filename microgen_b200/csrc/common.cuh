@@ -11,6 +11,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/microgen_b200.h"
 
 #define MG_SPIN_LIMIT (1u << 22)
@@ -46,14 +48,21 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 
 bool mg_pdl_enabled();
 
-// True the first time it is called for `flags` on the current device (function attributes such as
-// the dynamic shared-memory limit belong to the current device's copy of the kernel).
-inline bool mg_first_on_device(bool (&flags)[64]) {
+// Runs `setup` (returning a cudaError_t) once per device for one `flags` array: function attributes
+// such as the dynamic shared-memory limit belong to the current device's copy of a kernel. Threads
+// that get here first on a device wait for the set-up under a lock; the device is only marked done
+// after `setup` succeeded, so a failed set-up is retried by the next call.
+template <typename F>
+inline cudaError_t mg_once_per_device(bool (&flags)[64], std::mutex& mu, F&& setup) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
-  if (flags[dev]) return false;
-  flags[dev] = true;
-  return true;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return setup();
+  std::lock_guard<std::mutex> lock(mu);
+  if (flags[dev]) return cudaSuccess;
+  e = setup();
+  if (e == cudaSuccess) flags[dev] = true;
+  return e;
 }
 
 // Host: a 2-D tiled TMA descriptor (row-major [outer][inner], row_bytes apart; box_inner x box_outer).
@@ -105,6 +114,7 @@ struct PeerOut {
   uint32_t* count;                 // this rank: all-reduces pushed so far (= epoch of the last one)
   uint32_t* done;                  // this rank: CTAs finished in the push under way
   int64_t slot;                    // words (value pairs) per (set, rank) slot
+  uint64_t timeout_ns;             // how long a reduce waits for a peer's words before giving up
   int rank, world;
 };
 

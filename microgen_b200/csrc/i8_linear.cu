@@ -565,8 +565,10 @@ int launch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
               bool packed, const PeerOut* po) {
   using C = TcCfg<MP>;
   static bool attr_done[64] = {};
-  if (mg_first_on_device(attr_done))
-    MG_CUDA_TRY(cudaFuncSetAttribute(i8_gemm_tc<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+  static std::mutex attr_mu;
+  MG_CUDA_TRY(mg_once_per_device(attr_done, attr_mu, [] {
+    return cudaFuncSetAttribute(i8_gemm_tc<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  }));
   CUtensorMap mw, mx;
   const uint64_t packed_rows = (uint64_t)((n + kBN - 1) / kBN) * ((k + kBK - 1) / kBK) * kBN;
   int rc = packed ? make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, kBK, packed_rows, kBK, kBK, kBN)

@@ -302,6 +302,13 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
   for (int i = 0; i < kO; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
   if (warp == kProd) {
+    // Shared-prefix blocks are read from sequence 0's table: one CTA per sequence checks that its
+    // leading entries are the same blocks and records MG_ERR_DEVICE (site 403) when they are not.
+    if (p.n_shared > 0 && seq > 0 && h == 0 && sp == 0) {
+      bool same = true;
+      for (int i = lane; i < p.n_shared; i += 32) same &= table[i] == p.tables[i];
+      if (!__all_sync(0xffffffffu, same) && lane == 0) mg_record_error(MG_ERR_DEVICE, 403);
+    }
     // Block-table entries 32 at a time, one per lane, the next window loaded a window ahead.
     auto entry = [&](int i) { return i < ntiles ? table[b0 + i] : 0; };
     int cur = entry(lane), nxt = entry(32 + lane);
@@ -443,7 +450,12 @@ __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUt
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   for (int i = 0; i < nb; ++i) {
-    if (!mbar_wait(&full[i], 0, 412)) return;
+    if (!mbar_wait(&full[i], 0, 412)) {
+      // timed out (MG_ERR_TIMEOUT recorded): leave an empty state so the merge gives this slot no weight
+      m[0] = m[1] = -INFINITY;
+      l[0] = l[1] = 0.f;
+      break;
+    }
     const uint32_t ks = smem_u32(smem + i * C::kStageBytes);
     attend_tile<D>(qa, ks, ks + C::kTileBytes, 16, o, m, l, lane);
   }
@@ -561,12 +573,14 @@ template <int D>
 int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v_pool, cudaStream_t st) {
   using C = AttnCfg<D>;
   static bool attr_done[64] = {};
-  if (mg_first_on_device(attr_done)) {
-    MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     C::kSmem));
-    MG_CUDA_TRY(cudaFuncSetAttribute(paged_attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     C::kSmem));
-  }
+  static std::mutex attr_mu;
+  MG_CUDA_TRY(mg_once_per_device(attr_done, attr_mu, [] {
+    cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(paged_attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    return e;
+  }));
   // Pools as 2-D tensors [num_blocks*hkv*16 rows, D]: rows of one (block, kv head) tile are adjacent.
   const uint64_t rows = (uint64_t)p.num_blocks * p.hkv * 16;
   if (rows > 0x7fffffffull) return MG_ERR_UNSUPPORTED;

@@ -272,9 +272,20 @@ class DecodeEngine:
         # fused reduce(+norm) kernel finishes the all-reduce (MG_FUSED_AR=0 falls back to NCCL).
         self.comm = None
         # (the push epilogue works on whole 128-row output tiles: hidden % 128 == 0, else NCCL)
-        if (world > 1 and os.environ.get("MG_FUSED_AR", "1") != "0" and isinstance(weights.lm_q, K.PackedWeight)
-                and spec.hidden % 128 == 0 and spec.hidden <= 8192):
+        if world > 1 and self.fused_allreduce_choice(group) and isinstance(weights.lm_q, K.PackedWeight) \
+                and spec.hidden % 128 == 0 and spec.hidden <= 8192:
             self.comm = K.Comm(rank, world, max_batch * spec.hidden, group=group)
+
+    @staticmethod
+    def fused_allreduce_choice(group=None) -> bool:
+        """Whether the row-parallel linears reduce through the fused peer-memory push (MG_FUSED_AR unset or
+        not "0") or NCCL. Decided by the group's first rank and broadcast, so every rank takes the same path
+        even when their environments differ (a mix of the two paths would wait on pushes that never come)."""
+        want = [os.environ.get("MG_FUSED_AR", "1") != "0"]
+        import torch.distributed as dist
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(want, src=src, group=group)
+        return bool(want[0])
 
     # ---- the step -----------------------------------------------------------------------------
     def _norm(self, h, w, b, x):
@@ -323,7 +334,8 @@ class DecodeEngine:
                                  self.hkv, self.D, self.pool.k[l], self.pool.v[l], q_out=self.q[:b])
             with P("paged_attn", attn_bytes):
                 K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
-                                    n_shared_blocks=n_shared_blocks, out=self.attn[:b], workspace=self.workspace)
+                                    n_shared_blocks=n_shared_blocks, out=self.attn[:b], workspace=self.workspace,
+                                    validate=False)
             if fused:
                 with P("i8_linear", self.linear_bytes(L.o_q, b, 0, H) + push_bytes):
                     K.i8_linear_rowpar(self.attn[:b], L.o_q, L.o_s, self.comm)

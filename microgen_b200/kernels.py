@@ -145,9 +145,15 @@ def attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks=0) -> int:
 
 
 def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared_blocks=0, out=None,
-                      workspace=None):
+                      workspace=None, validate=True):
     """q fp32 [b, hq, d]; pools bf16 [nblk, hkv, 16, d]; tables int32 [b, max_blocks]; ctx int32 [b].
-    Returns bf16 [b, hq*d]."""
+    Returns bf16 [b, hq*d].
+
+    With ``n_shared_blocks`` > 0 the first that many entries of every table must equal row 0's (the
+    kernel reads the shared blocks once, from row 0); ``validate`` checks this before the launch and raises
+    ValueError (a device-to-host read: skipped while a CUDA graph is being captured; callers that check
+    their host copy of the tables pass False). The kernel also records MG_ERR_DEVICE when it sees a
+    mismatch."""
     _need(q, torch.float32, "q")
     _need(k_pool, torch.bfloat16, "k_pool")
     _need(v_pool, torch.bfloat16, "v_pool")
@@ -156,6 +162,9 @@ def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared
     b, hq, d = q.shape
     hkv = k_pool.shape[1]
     max_blocks = block_tables.shape[1]
+    if validate and n_shared_blocks > 0 and b > 1 and not torch.cuda.is_current_stream_capturing():
+        from .runtime.paged_kv import check_shared_prefix
+        check_shared_prefix(block_tables[:, :n_shared_blocks].cpu().numpy(), n_shared_blocks)
     ws = attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks)
     if ws and (workspace is None or workspace.numel() * workspace.element_size() < ws):
         workspace = torch.empty(ws, dtype=torch.uint8, device=q.device)

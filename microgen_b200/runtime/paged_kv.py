@@ -185,11 +185,27 @@ class TableMirror:
                     or (n and self.arr[i, n - 1] != blocks[n - 1].block_id)):
                 self.arr[i, :n] = 0
                 self._tabs[i], self._ver[i], n = t, t.version, 0
+                self._n[i] = 0
             if nb > n:
                 self.arr[i, n:nb] = [b.block_id for b in blocks[n:nb]]
-                self._n[i] = nb
+            self._n[i] = nb
             width = max(width, nb)
         return self.arr[:len(tables), :width]
+
+
+def check_shared_prefix(tables: np.ndarray, n_shared_blocks: int) -> None:
+    """Raise ValueError unless the first ``n_shared_blocks`` entries of every row of ``tables`` equal
+    row 0's: the attention kernel reads shared-prefix blocks once, from row 0's table."""
+    if n_shared_blocks <= 0 or len(tables) == 0:
+        return
+    t = np.asarray(tables)
+    if n_shared_blocks > t.shape[1]:
+        raise ValueError(f"{n_shared_blocks} shared blocks > table width {t.shape[1]}")
+    lead = t[:, :n_shared_blocks]
+    bad = np.nonzero((lead != lead[:1]).any(axis=1))[0]
+    if len(bad):
+        raise ValueError(f"n_shared_blocks={n_shared_blocks}, but the leading block ids of sequence {int(bad[0])} "
+                         "differ from sequence 0's: shared-prefix blocks must be the same in every table")
 
 
 def block_table_tensor(tables: Sequence[BlockTable], max_blocks: int, device=None) -> torch.Tensor:

@@ -24,9 +24,9 @@ TINY = {
 }
 
 
-def seeded_state(model: torch.nn.Module, seed: int) -> dict:
+def _seeded_params(model: torch.nn.Module, seed: int):
+    """(name, numpy fp32 value) of every parameter in ``named_parameters`` order, drawn from one PCG64."""
     rng = np.random.default_rng(seed)
-    out = {}
     for name, p in model.named_parameters():
         leaf = name.rsplit(".", 1)[0].rsplit(".", 1)[-1]
         if name.endswith("bias"):
@@ -34,9 +34,39 @@ def seeded_state(model: torch.nn.Module, seed: int) -> dict:
         elif "norm" in leaf or leaf.startswith("ln_"):
             a = np.ones(p.shape, np.float32)
         else:
-            a = (rng.standard_normal(p.shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
-        out[name] = a
-    return out
+            a = rng.standard_normal(p.shape, dtype=np.float32)
+            a *= np.float32(0.02)
+        yield name, a
+
+
+def seeded_state(model: torch.nn.Module, seed: int) -> dict:
+    return dict(_seeded_params(model, seed))
+
+
+def seeded_model(shape: dict, seed: int = 0):
+    """HF model of ``shape`` (fp32, eval) with the seeded weights, filled one parameter at a time
+    (no second copy of the weights is held: full-size shapes fit in host memory)."""
+    from transformers import AutoModelForCausalLM
+    cfg = hf_config(shape)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    model = AutoModelForCausalLM.from_config(cfg)
+    params = dict(model.named_parameters())
+    with torch.no_grad():
+        for name, a in _seeded_params(model, seed):
+            params[name].copy_(torch.from_numpy(a))
+    return model.eval()
+
+
+def seeded_state_for_shape(shape: dict, seed: int = 0) -> tuple[object, dict]:
+    """(HF config, {parameter name: fp32 CPU tensor}) with exactly the values ``seeded_model`` holds,
+    without building the HF model's weights (the parameter order comes from a meta-device model)."""
+    from transformers import AutoModelForCausalLM
+    cfg = hf_config(shape)
+    cfg._attn_implementation = "sdpa"
+    with torch.device("meta"):
+        model = AutoModelForCausalLM.from_config(cfg)
+    return cfg, {name: torch.from_numpy(a) for name, a in _seeded_params(model, seed)}
 
 
 def make_hf_model(shape: dict, seed: int = 0):

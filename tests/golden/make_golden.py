@@ -1,10 +1,10 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE itself.
 
-Run in the build container, where the reference checkout and transformers 5.5.0
-are importable (``MICROGEN_REFERENCE`` points at the checkout, default
-``/root/reference``)::
+Run where the reference checkout and transformers 5.5.0 are importable;
+``MICROGEN_REFERENCE`` must point at the checkout::
 
-    python tests/golden/make_golden.py
+    MICROGEN_REFERENCE=<checkout> python tests/golden/make_golden.py          # small fixtures
+    MICROGEN_REFERENCE=<checkout> python tests/golden/make_golden.py --full   # full-shape streams
 
 Every array written here is an output of the reference's own code:
 
@@ -27,6 +27,11 @@ Every array written here is an output of the reference's own code:
   ``prefill``/``decode`` on seeded tiny Llama / Qwen2 / GPT-2 models. For GPT-2
   the Conv1D projections are first rewrapped as ``nn.Linear`` (weight =
   ``Conv1D.weight.T``), because the reference quantizer only swaps ``nn.Linear``.
+* ``full_<shape>.npz`` (``--full``) — the same greedy stream at the full model
+  shapes of the workloads (GPT-2-small, Qwen2.5-0.5B, Llama-3.2-3B; every layer,
+  the full vocabulary) for a batch of two prompts: 64 greedy tokens per sequence,
+  the reference's top-1 minus top-2 logit margin at every step, and a sample of
+  the logits of the first steps (a fixed strided index set plus each row's top 16).
 """
 
 from __future__ import annotations
@@ -42,7 +47,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("MICROGEN_REFERENCE", "/root/reference")
+REF = os.environ.get("MICROGEN_REFERENCE")
+if not REF:
+    sys.exit("set MICROGEN_REFERENCE to the MicroGen checkout whose code produces the fixtures")
 sys.path.insert(0, REF)
 sys.path.insert(0, ROOT)  # this repository's ``tests`` package wins over the reference's
 
@@ -220,6 +227,41 @@ def make_alloc_trace():
         json.dump(trace, f, indent=1)
 
 
+def make_prefix_trace():
+    """Scripted insert / match / evict / get sequence on the reference's PrefixKVCache (capacity 3); each
+    stored state is a label, so the trace records which entry every lookup returns."""
+    from microgen.caching.prefix_cache import PrefixKVCache, compute_token_hash
+    pc = PrefixKVCache(max_capacity=3)
+    seqs = {"a": list(range(1, 33)), "b": list(range(1, 17)), "c": [7] * 16 + [9] * 16, "d": list(range(1, 49)),
+            "e": [3] * 16}
+    trace = []
+    keys = {}
+
+    def match(ids):
+        m = pc.match_prefix(ids)
+        return None if m is None else [m[0], m[1]]
+
+    for lab in ("a", "b", "c"):
+        keys[lab] = pc.insert(seqs[lab], lab)
+        trace.append(["insert", lab, keys[lab], pc.size])
+    for probe in (list(range(1, 41)), list(range(1, 21)), [7] * 16 + [9] * 20, [2, 3], list(range(1, 16)), []):
+        trace.append(["match", probe, match(probe)])
+    keys["d"] = pc.insert(seqs["d"], "d")           # evicts "a" (oldest)
+    trace.append(["insert", "d", keys["d"], pc.size])
+    trace.append(["get", "a", pc.get(keys["a"])])
+    trace.append(["get", "b", pc.get(keys["b"])])
+    trace.append(["match", list(range(1, 41)), match(list(range(1, 41)))])
+    trace.append(["match", list(range(1, 60)), match(list(range(1, 60)))])
+    keys["b2"] = pc.insert(seqs["b"], "b2")        # re-insert of a present key: no eviction
+    trace.append(["insert", "b2", keys["b2"], pc.size])
+    keys["e"] = pc.insert(seqs["e"], "e")           # evicts "b" (the oldest remaining insertion)
+    trace.append(["insert", "e", keys["e"], pc.size])
+    trace.append(["match", list(range(1, 20)), match(list(range(1, 20)))])
+    trace.append(["hash", [1, 2, 3], compute_token_hash([1, 2, 3])])
+    with open(os.path.join(HERE, "prefix_trace.json"), "w") as f:
+        json.dump({"seqs": seqs, "trace": trace}, f, indent=0)
+
+
 def _conv1d_to_linear(model):
     from transformers.pytorch_utils import Conv1D
 
@@ -258,10 +300,69 @@ def make_models(n_prompt=16, n_new=64, n_logits=8):
                             shape=json.dumps(shape))
 
 
+# Full-shape greedy streams: batch of two prompts of FULL_PROMPT ids; the Llama-3.2-3B shape shares
+# its first FULL_SHARED ids across the batch (the shared-prefix workload), the others share nothing.
+FULL_PROMPT, FULL_SHARED, FULL_NEW, FULL_LOGIT_STEPS, FULL_STRIDE, FULL_TOPK = 40, 32, 64, 4, 61, 16
+
+
+def full_prompts(vocab: int, shared: int) -> list[list[int]]:
+    head = prompt_ids(vocab, shared, seed=50) if shared else []
+    return [head + prompt_ids(vocab, FULL_PROMPT - shared, seed=51 + i) for i in range(2)]
+
+
+def make_full_models(names=("GPT2_SMALL", "QWEN_05B", "LLAMA_3B")):
+    import gc
+    import time
+    from microgen_b200 import model_spec as MS
+    from tests._hf_models import seeded_model
+    for name in names:
+        t0 = time.time()
+        shape = dict(getattr(MS, name))
+        shared = FULL_SHARED if name == "LLAMA_3B" else 0
+        model = seeded_model(shape, seed=0)
+        if shape["family"] == "gpt2":
+            _conv1d_to_linear(model)
+        be = QuantizedPyTorchBackend(quant_type="int8")
+        be.load_model(name, model_instance=model)
+        gc.collect()
+        prompts = full_prompts(shape["vocab"], shared)
+        ids = torch.tensor(prompts, dtype=torch.long)
+        V = shape["vocab"]
+        idx = np.arange(0, V, FULL_STRIDE, dtype=np.int64)
+        toks, margins, vals, top_i, top_v = [], [], [], [], []
+        with torch.no_grad():
+            logits, cache = be.prefill(ids, cache=KVCacheState(max_seq_len=4096))
+            for i in range(FULL_NEW):
+                lg = logits.float()
+                tok = torch.argmax(lg, dim=-1, keepdim=True)
+                t2 = torch.topk(lg, 2, dim=-1).values
+                toks.append(tok[:, 0].numpy().copy())
+                margins.append((t2[:, 0] - t2[:, 1]).numpy().copy())
+                if i < FULL_LOGIT_STEPS:
+                    vals.append(lg[:, idx].numpy().copy())
+                    tk = torch.topk(lg, FULL_TOPK, dim=-1)
+                    top_i.append(tk.indices.numpy().copy())
+                    top_v.append(tk.values.numpy().copy())
+                logits, cache = be.decode(tok, cache=cache)
+        np.savez_compressed(
+            os.path.join(HERE, f"full_{name.lower()}.npz"), prompts=np.array(prompts, np.int64),
+            shared=np.int64(shared), tokens=np.stack(toks, 1).astype(np.int64),
+            margins=np.stack(margins, 1).astype(np.float32), logit_idx=idx,
+            logit_val=np.stack(vals, 1).astype(np.float32), top_idx=np.stack(top_i, 1).astype(np.int64),
+            top_val=np.stack(top_v, 1).astype(np.float32), shape=json.dumps(shape))
+        print(f"{name}: {time.time() - t0:.0f} s; min margin {np.min(np.stack(margins)):.4f}", flush=True)
+        del be, model, cache, logits
+        gc.collect()
+
+
 if __name__ == "__main__":
+    if "--full" in sys.argv:
+        make_full_models([a for a in sys.argv[1:] if a != "--full"] or ("GPT2_SMALL", "QWEN_05B", "LLAMA_3B"))
+        sys.exit(0)
     make_quant()
     make_linear()
     make_attn()
     make_alloc_trace()
+    make_prefix_trace()
     make_models()
     print("golden fixtures written to", HERE)

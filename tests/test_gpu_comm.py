@@ -83,3 +83,27 @@ def test_missing_peer_times_out_and_context_survives():
     finally:
         comm.close()
     test_world1_push_reduce_norm(1)  # the context is still healthy
+
+
+def test_decode_raises_when_a_peer_never_pushes():
+    """The serving path surfaces a peer timeout: a TP decode step whose row-parallel reduces wait on a rank
+    that never pushes (a world-2 communicator whose second rank maps to this process) ends in TimeoutError
+    from ``decode`` rather than returning logits built from missing partials."""
+    from microgen_b200 import kernels as K
+    from microgen_b200.backends import B200QuantizedBackend
+    from tests._hf_models import TINY, make_hf_model
+    model, _ = make_hf_model(TINY["llama"], seed=0)
+    be = B200QuantizedBackend(max_batch=1, max_seq_len=64, use_cuda_graph=False)
+    be.load_model("tiny", model_instance=model)
+    logits, cache = be.prefill(torch.tensor([[1, 2, 3]]))
+    K.check_device()
+    comm = K.Comm(0, 2, be.engine.max_batch * be.spec.hidden, exchange=lambda mine: [mine, mine])
+    be.engine.comm = comm
+    try:
+        with pytest.raises(TimeoutError):
+            be.decode(be.sample(logits), cache=cache)
+    finally:
+        be.engine.comm = None
+        torch.cuda.synchronize()
+        comm.close()
+    test_world1_push_reduce_norm(1)  # the context is still healthy

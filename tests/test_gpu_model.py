@@ -134,3 +134,57 @@ def test_memory_usage_and_errors():
     with pytest.raises(ValueError):
         for _ in range(80):  # past max_seq_len
             logits, cache = be.decode(torch.tensor([[1]]), cache=cache)
+
+
+def _hf_last_logits(model, prompt):
+    with torch.no_grad():
+        out = model(input_ids=torch.tensor([prompt], device="cuda"), use_cache=False)
+    return out.logits[0, -1].float().cpu().numpy()
+
+
+def _oracle_last_logits(family, prompt):
+    _, om = _oracle(family)
+    c = om.new_cache()
+    lg = None
+    for t, tok in enumerate(prompt):
+        lg = om.step(tok, t, c)
+    return lg
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+def test_quantize_model_swaps_every_linear(family):
+    """quantize_model (quantized.py:59-73): every nn.Linear of an HF model becomes a QuantizedLinear on the
+    INT8 kernel; the model's own forward then matches the oracle's INT8 model."""
+    from microgen_b200.backends import QuantizedLinear, quantize_model
+    model, _ = make_hf_model(TINY[family], seed=0)
+    model = model.cuda()
+    n_linear = sum(isinstance(m, torch.nn.Linear) for m in model.modules())
+    quantize_model(model)
+    assert not any(isinstance(m, torch.nn.Linear) for m in model.modules())
+    assert sum(isinstance(m, QuantizedLinear) for m in model.modules()) == n_linear
+    prompt = prompt_ids(TINY[family]["vocab"], 12, seed=4)
+    close(_hf_last_logits(model, prompt), _oracle_last_logits(family, prompt))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_apply_tensor_parallelism_walk(world):
+    """apply_tensor_parallelism (parallel.py:108-131): q/k/v/gate/up become INT8 column-parallel and o/down
+    row-parallel by child name, lm_head is left alone; with lm_head then quantized, the HF forward matches the
+    oracle's INT8 model."""
+    from microgen_b200.backends import (ColumnParallelLinear, RowParallelLinear, apply_tensor_parallelism,
+                                        quantize_model)
+    model, _ = make_hf_model(TINY["llama"], seed=0)
+    model = model.cuda()
+    apply_tensor_parallelism(model, world)
+    layer = model.model.layers[0]
+    for n in ("q_proj", "k_proj", "v_proj"):
+        assert isinstance(getattr(layer.self_attn, n), ColumnParallelLinear)
+    assert isinstance(layer.self_attn.o_proj, RowParallelLinear)
+    assert isinstance(layer.mlp.gate_proj, ColumnParallelLinear) and isinstance(layer.mlp.up_proj,
+                                                                                   ColumnParallelLinear)
+    assert isinstance(layer.mlp.down_proj, RowParallelLinear)
+    assert isinstance(model.lm_head, torch.nn.Linear)  # unmatched: stays as it is
+    assert len(layer.self_attn.q_proj.shards) == world
+    quantize_model(model)  # lm_head -> INT8, as in the oracle model
+    prompt = prompt_ids(TINY["llama"]["vocab"], 12, seed=6)
+    close(_hf_last_logits(model, prompt), _oracle_last_logits("llama", prompt))

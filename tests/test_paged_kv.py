@@ -103,3 +103,33 @@ def test_table_mirror_rejects_oversized_input():
         m.update([a.allocate_sequence("x", 16 * 5)])
     with pytest.raises(ValueError):
         m.update([a.allocate_sequence(f"y{i}", 1) for i in range(3)])
+
+
+def test_table_mirror_row_reused_by_an_empty_table_then_block_zero():
+    """A row that held 3 blocks gets a new empty table, which then grows to 3 blocks whose last id is 0:
+    the mirror must hold the new ids, not the zeros left by the rebuild."""
+    a = PagedKVCacheAllocator(num_blocks=8, block_size=16)
+    old = a.allocate_sequence("old", 40)  # blocks 0, 1, 2
+    m = TableMirror(1, 8)
+    assert m.update([old])[0].tolist() == [0, 1, 2]
+    a.free_sequence(old)
+    a._free_blocks.sort(key=lambda b: -b.block_id)  # hand out 7, 6, ..., 0 so the third block is 0
+    a._free_blocks = [b for b in a._free_blocks if b.block_id in (5, 3, 0)]
+    new = a.allocate_sequence("new", 0)
+    assert m.update([new]).shape == (1, 0)
+    for _ in range(33):
+        a.append_token(new)
+    assert [b.block_id for b in new.physical_blocks] == [5, 3, 0]
+    assert m.update([new])[0].tolist() == [5, 3, 0]
+
+
+def test_check_shared_prefix():
+    from microgen_b200.runtime.paged_kv import check_shared_prefix
+    t = np.array([[4, 7, 1, 0], [4, 7, 2, 3], [4, 7, 5, 6]], np.int32)
+    check_shared_prefix(t, 2)
+    check_shared_prefix(t, 0)
+    with pytest.raises(ValueError):
+        check_shared_prefix(t, 3)
+    t[2, 1] = 9
+    with pytest.raises(ValueError, match="sequence 2"):
+        check_shared_prefix(t, 2)
