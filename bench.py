@@ -85,7 +85,7 @@ def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps:
 
     def run_lin():
         for x, q, sc, bias, y, e, _ in lin:
-            K.i8_linear(x, q, sc, bias, y=y, epilogue=e)
+            K.i8_linear(x, q, sc, bias, y=y, epilogue=e, workspace=eng.lin_ws)
 
     def run_attn():
         for l in range(len(w.layers)):
@@ -130,9 +130,9 @@ def push_chain(eng, spec, b: int, reps: int = 10) -> dict:
 
     def run():
         for L in eng.w.layers:
-            K.i8_linear_rowpar(eng.attn[:b], L.o_q, L.o_s, eng.comm)
+            K.i8_linear_rowpar(eng.attn[:b], L.o_q, L.o_s, eng.comm, workspace=eng.lin_ws)
             K.rowpar_reduce_norm(eng.comm, scratch, None, K.NORM_NONE)
-            K.i8_linear_rowpar(eng.act[:b], L.d_q, L.d_s, eng.comm)
+            K.i8_linear_rowpar(eng.act[:b], L.d_q, L.d_s, eng.comm, workspace=eng.lin_ws)
             K.rowpar_reduce_norm(eng.comm, scratch, None, K.NORM_NONE)
 
     dist.barrier()
@@ -231,6 +231,7 @@ def sweep_c4(args) -> None:
     comm = None
     if world > 1:
         comm = K.Comm(rank, world, max(C4_M) * max(n for _, n in C4_LINEAR))
+    skws = K.sk_workspace(128, dev)  # stream-K form for M <= 128 (larger M runs the cluster kernel)
     for k, n in C4_LINEAR:
         w = torch.randn((n, k), generator=g, device=dev).mul_(0.02)
         q, s = K.quantize_rows_i8(w)
@@ -248,10 +249,14 @@ def sweep_c4(args) -> None:
                     "bytes": k * n + 4 * n + 2 * m * k + 2 * m * n, "peak_gbs": hbm, "peak_source": hbm_kind,
                     "l2": "flushed before every launch"}
             if world == 1:
+                us_sk = _timed(lambda: K.i8_linear(x, qp, s, y=y, epilogue=K.EPI_STORE_BF16, workspace=skws), reps,
+                               flush) if skws is not None else None
                 us_tc = _timed(lambda: K.i8_linear(x, qp, s, y=y, epilogue=K.EPI_STORE_BF16), reps, flush)
                 us_simt = _timed(lambda: K.i8_linear(x, q, s, y=y, epilogue=K.EPI_STORE_BF16, algo="simt"), reps,
                                  flush)
-                for name, us in (("tc", us_tc), ("simt", us_simt)):
+                for name, us in (("tc_streamk", us_sk), ("tc", us_tc), ("simt", us_simt)):
+                    if us is None:
+                        continue
                     gbs = line["bytes"] / us / 1e3
                     line[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4)}
             else:
@@ -308,7 +313,7 @@ def sweep_c4(args) -> None:
             tab = tables.to(dev)
             ctxs = torch.full((b,), ctx, dtype=torch.int32, device=dev)
             out = torch.empty((b, hq * d), dtype=torch.bfloat16, device=dev)
-            ws = torch.empty(max(16, K.attn_workspace_bytes(b, hq, hkv, d, nb, ns)), dtype=torch.uint8, device=dev)
+            ws = torch.zeros(max(16, K.attn_workspace_bytes(b, hq, hkv, d, nb, ns)), dtype=torch.uint8, device=dev)
             us = _timed(lambda: K.paged_decode_attn(qq, kp, vp, tab, ctxs, d ** -0.5, n_shared_blocks=ns, out=out,
                                                     workspace=ws, validate=False), reps, flush)
             nbytes = (ns * 16 + b * (ctx - ns * 16)) * hkv * d * 2 * 2 + b * hq * d * (4 + 2)
@@ -397,25 +402,45 @@ def cpu_baseline(spec, wl, ctx, budget_s=20.0) -> dict:
                        f"({r['head_s']:.3f} s); step = {spec.layers} x layer + head = {r['step_s']:.2f} s")}
 
 
+def workload_config(name: str, wl: dict, world: int) -> dict:
+    """The workload both arms report (identical keys and values): model shape, batch, prompt, shared
+    prefix, decode length and the mean context of the timed window."""
+    mean_ctx = wl["prompt"] + wl["decode"] // 2
+    return {"workload": f"{name}: {wl['shape']} INT8, batch {wl['batch']}, prompt {wl['prompt']} "
+                        f"({wl['shared']} shared), decode {wl['decode']}; timed at mean ctx {mean_ctx}",
+            "batch": wl["batch"], "prompt": wl["prompt"], "shared_prefix": wl["shared"], "decode": wl["decode"],
+            "mean_ctx": mean_ctx, "tp": world, "parallelism": f"tp{world}"}
+
+
 def run_reference(args) -> None:
-    """The reference arm: the reference path is Python on the host CPU; it cannot be installed
-    on the GPU box, so its restatement (the oracle port) is timed on the host cores."""
+    """The reference arm: the reference's decode path is Python on the host CPU (fp32, dequantize-per-call
+    linears, cat-grown cache); its numpy restatement (the oracle port) runs WHOLE decode steps of the
+    workload on the host cores, warm-up then as many timed steps as fit in the time budget, and the line
+    reports the steps it actually timed. Under torchrun only rank 0 runs it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from microgen_b200 import model_spec as MS
+    from oracle.cpu_baseline import measure_steps
     wl = WORKLOADS[args.workload]
     spec = MS.ModelSpec(**getattr(MS, wl["shape"]))
     ctx = wl["prompt"] + wl["decode"] // 2
-    budget = min(90.0, max(10.0, 2.0 * (args.steps + args.warmup)))
-    cb = cpu_baseline(spec, wl, ctx, budget_s=budget)
-    v = cb["value"]
+    budget = float(os.environ.get("MG_REFERENCE_BUDGET_S", "60"))
+    r = measure_steps(spec.hidden, spec.heads, spec.kv_heads, spec.head_dim, spec.inter, spec.vocab, spec.layers,
+                      wl["batch"], ctx, budget_s=budget, max_steps=max(1, args.steps), warmup=1, eps=spec.eps,
+                      theta=spec.rope_theta)
+    v = round(r["tokens_per_s"], 4)
+    sample = (f"numpy fp32 restatement of the reference CPU decode step (dequantize-per-call linears, cat-grown "
+              f"cache, SDPA) at the full {wl['shape']} shape, batch {wl['batch']}, ctx {ctx}: {r['steps']} whole "
+              f"steps ({spec.layers} layers + lm_head) timed after {r['warmup']} warm-up step, "
+              f"{r['timed_s']:.1f} s; {args.steps} requested, bounded by a {budget:.0f} s budget")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * wl["batch"] / v, 3),
+        "steps": r["steps"], "warmup": r["warmup"], "ms_per_step": round(1000.0 * r["step_s"], 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {wl}", "tp": 1, "device": "host cpu"},
-        "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": workload_config(args.workload, wl, args.gpus),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": r["threads"], "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
@@ -682,11 +707,10 @@ def main():
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": Kst,
         "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 weights x bf16 activations, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {wl['shape']} INT8, batch {B}, prompt {P} ({S} shared), decode "
-                               f"{Dec}; timed window mean ctx {mean_pos + 1:.0f}",
-                   "batch": B, "prompt": P, "shared_prefix": S, "tp": world, "parallelism": f"tp{world}",
-                   "l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True,
-                   "row_parallel_reduce": reduce_kind},
+        "config": workload_config(args.workload, wl, world),
+        "setup": {"l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True,
+                  "row_parallel_reduce": reduce_kind, "linear_kernel": "stream-K" if eng.lin_ws is not None
+                  else "cluster split-K", "timed_window_mean_ctx": round(mean_pos + 1)},
         "roofline": roofline, "step_roofline": step_roofline, "kernel_chains": chains, "nvlink": nvlink,
         "kernels": kernels,
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst,

@@ -82,6 +82,19 @@ int mg_i8_pack_weights(const int8_t* q, int64_t n, int64_t k, int8_t* packed, vo
 int mg_i8_linear_packed(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed, const float* scales,
                         const float* bias, int64_t n, void* y, int64_t ldy, int epilogue, int split_k, void* stream);
 
+/* Stream-K form of mg_i8_linear_packed (quantized.py:24-27; the shards of parallel.py:34-37), used by the
+ * decode engine for m <= 128 tokens: one wave of CTAs, each streaming an equal contiguous run of the
+ * packed weight's (128-row tile, 128-column block) units; tiles shared by several CTAs are finished by the
+ * CTA holding their first block, which adds the others' fp32 partials in CTA order (bit-reproducible).
+ * workspace: device memory of at least mg_i8_linear_sk_workspace_bytes(m) bytes, 256-byte aligned,
+ * zero-filled before its first use; every launch leaves it as it found it, so one workspace serves any
+ * stream-ordered sequence of calls (calls that overlap on the GPU need separate workspaces).
+ * m > 128 runs the cluster kernel of mg_i8_linear_packed (the workspace is then unused). */
+int64_t mg_i8_linear_sk_workspace_bytes(int64_t m);
+int mg_i8_linear_packed_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                           const float* scales, const float* bias, int64_t n, void* y, int64_t ldy, int epilogue,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- fused row-parallel all-reduce over peer memory (parallel.py:65-81 + its "all-reduce") ---------
  * One communicator per rank of a tensor-parallel group (world <= 8, one process per GPU):
  *   mg_comm_create  allocates this rank's receive area (2 sets x world x slot_elems/2 64-bit words) and
@@ -104,6 +117,10 @@ int mg_i8_linear_packed_rowpar(const void* x, int64_t m, int64_t k, int64_t ldx,
                                const float* scales, int64_t n, void* comm, int split_k, void* stream);
 int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, int m, int n, int norm, const float* w,
                           const float* wb, float eps, void* x, void* stream);
+/* mg_i8_linear_packed_rowpar on the stream-K kernel (workspace as for mg_i8_linear_packed_sk). */
+int mg_i8_linear_packed_rowpar_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                                  const float* scales, int64_t n, void* comm, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 
 /* ---- paged KV: RoPE + append (kv_cache.py:76-127, as one slot write per token) ------------ */
 /* qkv fp32 [b, (hq+2*hkv)*d] (row stride ld_qkv): q heads, then k heads, then v heads.
@@ -119,8 +136,13 @@ int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t* positions
  * h / (hq/hkv); K/V gathered through block_tables int32 [b, max_blocks] from pools
  * bf16 [num_blocks, hkv, 16, d]; ctx_lens int32 [b] >= 1. d in {32, 64, 128}; hq/hkv <= 16.
  * n_shared_blocks: the first n_shared_blocks entries of every table are the same blocks
- * (a shared prefix); they are read once per batch. 0 = no sharing.
- * workspace: device scratch of mg_paged_attn_workspace_bytes() bytes (may be NULL if 0). */
+ * (a shared prefix); they are read once per batch. 0 = no sharing. A table whose leading entries differ
+ * from row 0's is recorded as MG_ERR_DEVICE (site 403).
+ * workspace: device scratch of mg_paged_attn_workspace_bytes() bytes, 16-byte aligned (may be NULL if 0),
+ * zero-filled before its first use: its first 64 KB hold one merge ticket per (sequence, kv head), which the
+ * last CTA of the pair resets, so every launch leaves the tickets at zero and one workspace (large enough)
+ * serves launches of any shape; the split partials follow. b * hkv <= 16384 (else MG_ERR_UNSUPPORTED).
+ * One launch (no separate combine kernel) covers the whole attention. */
 int mg_paged_attn_workspace_bytes(int b, int hq, int hkv, int d, int max_blocks, int n_shared_blocks,
                                   size_t* bytes);
 int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
@@ -140,9 +162,10 @@ int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool,
  * make that first call before any stream capture. The address is kept for the life of the process:
  * after cudaDeviceReset (which unloads the library's device code) this entry point must not be called
  * again on that device. All calls share the array: calls whose kernels overlap on the GPU (e.g. on two
- * streams) race on it — serialise them. Nothing in it needs clearing: each call writes every slot it
- * later reads (a split whose bounded wait gave up writes an empty softmax state and records
- * MG_ERR_TIMEOUT). */
+ * streams) race on it — serialise them. Nothing in it needs clearing: each call writes every split slot
+ * it later reads (a split whose bounded wait gave up writes an empty softmax state and records
+ * MG_ERR_TIMEOUT), and the merge tickets, zero when the library loads, are left at zero by every call
+ * (every CTA counts itself in, on the error paths too). */
 #define MG_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
 int mg_paged_decode_attn_noalloc(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
                                  const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,

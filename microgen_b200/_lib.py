@@ -40,6 +40,9 @@ SIGNATURES = {
     "mg_i8_packed_bytes": [_i64, _i64],
     "mg_i8_pack_weights": [_p, _i64, _i64, _p, _p],
     "mg_i8_linear_packed": [_p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _i, _p],
+    "mg_i8_linear_sk_workspace_bytes": [_i64],
+    "mg_i8_linear_packed_sk": [_p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _i, _p, _sz, _p],
+    "mg_i8_linear_packed_rowpar_sk": [_p, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _sz, _p],
     "mg_comm_handle_bytes": [],
     "mg_comm_create": [_i, _i, _i64, C.POINTER(C.c_void_p), _p],
     "mg_comm_open": [_p, _p],
@@ -56,12 +59,14 @@ SIGNATURES = {
     "mg_argmax_rows": [_p, _i, _i64, _i64, _p, _p],
     "mg_decode_advance": [_p, _p, _p, _p, _p, _p, _i, _i, _p],
 }
-_RESTYPES = {"mg_status_string": C.c_char_p, "mg_i8_packed_bytes": C.c_int64}
+_RESTYPES = {"mg_status_string": C.c_char_p, "mg_i8_packed_bytes": C.c_int64,
+             "mg_i8_linear_sk_workspace_bytes": C.c_int64}
 
-# entry points that launch one kernel per call (mg_paged_decode_attn adds its combine kernel)
+# entry points that launch one kernel per call
 LAUNCHING = {"mg_quantize_rows_i8", "mg_i8_linear", "mg_i8_linear_simt", "mg_i8_linear_tc", "mg_rope_kv_append",
              "mg_i8_pack_weights", "mg_i8_linear_packed", "mg_paged_decode_attn_noalloc",
-             "mg_i8_linear_packed_rowpar", "mg_rowpar_reduce_norm",
+             "mg_i8_linear_packed_rowpar", "mg_rowpar_reduce_norm", "mg_i8_linear_packed_sk",
+             "mg_i8_linear_packed_rowpar_sk",
              "mg_paged_decode_attn", "mg_embed", "mg_rmsnorm", "mg_layernorm", "mg_argmax_rows",
              "mg_decode_advance"}
 LAUNCHES = [0]  # kernels launched (or captured) through call() in this process

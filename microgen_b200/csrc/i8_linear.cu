@@ -22,6 +22,7 @@
 //   shared memory and the cluster reduces it through distributed shared memory
 //   (fixed order, deterministic), applying scale, bias and the epilogue — or, for a
 //   row-parallel linear, pushing the tile into every rank's receive slot (comm.cu).
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -531,6 +532,401 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 }
 
 // ------------------------------------------------------------------------------------------------
+// Stream-K form of the tcgen05 kernel (tile-packed codes, m <= 128).
+//
+// The work of one launch is the list of units (weight tile t, K block kb) in the order u = t*KB + kb,
+// which is also the order of the tile-packed codes in memory. The grid is one resident wave of CTAs
+// (SMs x CTAs per SM, at most one CTA per two units) and CTA c streams the contiguous units
+// [c*U/G, (c+1)*U/G): every CTA gets the same number of weight bytes, so no SM idles on a short tile
+// count or a partial second wave, and no thread-block cluster or distributed shared memory is needed.
+//
+// A CTA's range is a sequence of segments (its units of one tile). The MMA warp accumulates a segment
+// in TMEM; at the segment's end the converter warps drain the accumulator into shared memory (the MMA
+// warp then starts the next segment) and
+//   * a segment that is the whole tile runs the epilogue directly;
+//   * a segment that does not start at the tile's first K block (only a CTA's first segment can be one)
+//     stores its fp32 partial in the workspace slot of this CTA and raises the CTA's flag;
+//   * a segment that starts the tile but ends before its last K block belongs to the tile's finisher:
+//     it waits for the flags of the following CTAs whose first segment lies in the tile, adds their
+//     partials in CTA order (the sum does not depend on timing) and runs the epilogue.
+// The finisher reaches such a tile at the end of its own range, the contributors at the start of theirs,
+// so the wait is normally already satisfied. All CTAs of the grid are resident together, so the waits
+// cannot deadlock; every wait is still bounded (MG_ERR_TIMEOUT). The finisher clears the flags it
+// consumed, so the workspace is left as it was found (zero flags): it must be zero-filled before its
+// first use and may be shared by any stream-ordered sequence of launches.
+// ------------------------------------------------------------------------------------------------
+template <int MP>
+struct SkCfg {
+  static constexpr int kCtasPerSm = MP <= 32 ? 2 : 1;
+  static constexpr int kWStages = MP <= 16 ? 5 : (MP <= 32 ? 4 : (MP <= 64 ? 8 : 6));
+  static constexpr int kXStages = MP <= 64 ? 3 : 2;
+  static constexpr int kABufs = MP <= 32 ? 3 : (MP <= 64 ? 6 : 4);
+  static constexpr uint32_t kXStageBytes = MP * kBK * 2;
+  static constexpr uint32_t kXOffset = kWStages * kWStageBytes;
+  static constexpr uint32_t kRedOffset = kXOffset + kXStages * kXStageBytes;
+  static constexpr uint32_t kRedBytes = MP * kBN * 4;
+  static constexpr uint32_t kBarOffset = kRedOffset + kRedBytes;
+  static constexpr uint32_t kSmemBytes = kBarOffset + 512 + 1024;  // barriers + alignment slack
+  static constexpr uint32_t kAccCol = kABufs * 64;
+  static constexpr uint32_t kTmemCols = kCtasPerSm == 2 ? 256 : 512;
+  static constexpr uint32_t kIdesc = TcCfg<MP>::kIdesc;
+  static_assert(kAccCol + (MP < 32 ? 32 : MP) <= kTmemCols, "TMEM columns");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static_assert(kCtasPerSm == 1 || 2 * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
+  static_assert((2 * kWStages + 2 * kXStages + 2 * kABufs + 2) * 8 + 4 <= 512, "barrier region");
+};
+
+__device__ __forceinline__ void conv_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Converter-warp barrier that also returns whether every converter thread passed `ok`.
+__device__ __forceinline__ bool conv_bar_and(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.and.pred q, 1, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int MP>
+__global__ void __launch_bounds__(kTcThreads, SkCfg<MP>::kCtasPerSm)
+    i8_gemm_sk(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, int M, int K,
+               int64_t N, const float* __restrict__ scales, const float* __restrict__ bias, void* y, int64_t ldy,
+               int epi, const PeerOut po, float* __restrict__ part, uint32_t* __restrict__ flags) {
+  using C = SkCfg<MP>;
+  constexpr int SW = C::kWStages;
+  constexpr int SX = C::kXStages;
+  constexpr int NA = C::kABufs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* wempty = wfull + SW;
+  uint64_t* xfull = wempty + SW;
+  uint64_t* xempty = xfull + SX;
+  uint64_t* afull = xempty + SX;
+  uint64_t* aempty = afull + NA;
+  uint64_t* accfull = aempty + NA;
+  uint64_t* accempty = accfull + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 1);
+  float* red = reinterpret_cast<float*>(smem + C::kRedOffset);
+  __shared__ int s_ok;  // the finisher's flag wait succeeded
+
+  griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = (K + kBK - 1) / kBK;
+  const int64_t U = ((N + kBN - 1) / kBN) * KB;
+  const int G = gridDim.x, cta = blockIdx.x;
+  auto ubeg = [&](int c) { return (int64_t)c * U / G; };
+  const int64_t u0 = ubeg(cta), u1 = ubeg(cta + 1);
+  const int nk = (int)(u1 - u0);
+  // segment boundaries: the segment containing stage i ends at stage seg_last(i)
+  auto seg_last = [&](int i) {
+    const int64_t tile_end = ((u0 + i) / KB + 1) * KB;
+    return (int)(min(u1, tile_end) - u0) - 1;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], kConvWarps);
+    }
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int b = 0; b < NA; ++b) {
+      mbar_init(&afull[b], kConvWarps);
+      mbar_init(&aempty[b], 1);
+    }
+    mbar_init(accfull, 1);
+    mbar_init(accempty, 1);
+    fence_mbar_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_holder, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      // Weight stages (the tile-packed unit u is the 16 KB block at row u*128) do not depend on the
+      // previous kernel and are issued before the dependency wait; activation stages after it.
+      bool ok = true;
+      int iw = 0, ix = 0;
+      for (; iw < nk && iw < SW; ++iw) {
+        mbar_arrive_expect_tx(&wfull[iw], kWStageBytes);
+        tma_load_2d(smem + iw * kWStageBytes, &tmap_w, &wfull[iw], 0, (int)((u0 + iw) * kBN));
+      }
+      griddep_wait();
+      uint32_t polls = 0;
+      while ((iw < nk || ix < nk) && ok) {
+        bool progressed = false;
+        if (ix < nk && (ix < SX || mbar_test_wait(&xempty[ix % SX], ((ix / SX) - 1) & 1))) {
+          const int s = ix % SX;
+          uint8_t* sx = smem + C::kXOffset + s * C::kXStageBytes;
+          const int k0 = (int)((u0 + ix) % KB) * kBK;
+          mbar_arrive_expect_tx(&xfull[s], C::kXStageBytes);
+          tma_load_2d(sx, &tmap_x, &xfull[s], k0, 0);
+          tma_load_2d(sx + MP * 128, &tmap_x, &xfull[s], k0 + 64, 0);
+          ++ix;
+          progressed = true;
+        }
+        if (iw < nk && mbar_test_wait(&wempty[iw % SW], ((iw / SW) - 1) & 1)) {
+          const int s = iw % SW;
+          mbar_arrive_expect_tx(&wfull[s], kWStageBytes);
+          tma_load_2d(smem + s * kWStageBytes, &tmap_w, &wfull[s], 0, (int)((u0 + iw) * kBN));
+          ++iw;
+          progressed = true;
+        }
+        if (!progressed) {
+          if (++polls > MG_SPIN_LIMIT) {
+            mg_record_error(MG_ERR_TIMEOUT, 11);
+            ok = false;
+          }
+          __nanosleep(32);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      bool ok = true;
+      int seg = 0;
+      for (int i = 0; i < nk && ok;) {
+        const int first = i, last = seg_last(i);
+        if (seg > 0) {  // the previous segment's accumulator has been drained
+          ok = mbar_wait(accempty, (seg - 1) & 1, 12);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        for (; i <= last && ok; ++i) {
+          const int s = i % SX, ab = i % NA;
+          ok = mbar_wait(&xfull[s], (i / SX) & 1, 13) && mbar_wait(&afull[ab], (i / NA) & 1, 14);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sx = smem_u32(smem + C::kXOffset + s * C::kXStageBytes);
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j) {
+            const uint32_t a_t = tmem + (uint32_t)(ab * 64 + j * 8);
+            const uint64_t bd = desc_sw128(sx + (uint32_t)((j >> 2) * MP * 128 + (j & 3) * 32));
+            tc_mma_ts(tmem + C::kAccCol, a_t, bd, C::kIdesc, (i > first || j > 0) ? 1u : 0u);
+          }
+          tc_commit(&xempty[s]);
+          tc_commit(&aempty[ab]);
+        }
+        if (ok) tc_commit(accfull);
+        ++seg;
+      }
+    }
+  } else {
+    // ---------------- converters, then each segment's epilogue ----------------
+    const int row = (warp & 3) * 32 + lane;
+    const int hh = warp >> 2;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const bool swiglu = epi == MG_EPI_SWIGLU_BF16;
+    const bool peer = epi == MG_EPI_PEER_F32;
+    const int t = threadIdx.x;
+    const int half = t >> 7;
+    const int r0 = swiglu ? (t & 63) : (t & 127);
+    const int m_valid = min(MP, M);
+    bool ok = true, waited = false;
+    uint32_t epoch = 0;
+    int seg = 0;
+    for (int i = 0; i < nk;) {
+      const int last = seg_last(i);
+      const int64_t useg = u0 + i;
+      const int64_t tile = useg / KB;
+      for (; i <= last; ++i) {
+        const int s = i % SW, ab = i % NA;
+        if (ok) ok = mbar_wait(&wfull[s], (i / SW) & 1, 15);
+        uint4 v[4];
+        if (ok) {
+          const uint8_t* src = smem + s * kWStageBytes + row * 128;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            v[c4] = *reinterpret_cast<const uint4*>(src + (((hh * 4 + c4) ^ (row & 7)) << 4));
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&wempty[s]);
+        if (ok && i >= NA) ok = mbar_wait(&aempty[ab], ((i / NA) - 1) & 1, 16);
+        if (ok) {
+          uint32_t r[32];
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            i8x4_to_bf16x4(v[c4].x, r[c4 * 8 + 0], r[c4 * 8 + 1]);
+            i8x4_to_bf16x4(v[c4].y, r[c4 * 8 + 2], r[c4 * 8 + 3]);
+            i8x4_to_bf16x4(v[c4].z, r[c4 * 8 + 4], r[c4 * 8 + 5]);
+            i8x4_to_bf16x4(v[c4].w, r[c4 * 8 + 6], r[c4 * 8 + 7]);
+          }
+          tmem_st32(tmem + lane_base + (uint32_t)(ab * 64 + hh * 32), r);
+          tc_wait_st();
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&afull[ab]);
+      }
+      // ---- segment epilogue: drain the accumulator into `red` [col][row] ----
+      if (ok) ok = mbar_wait(accfull, seg & 1, 17);
+      constexpr int kColsPerWarp = MP >= 64 ? MP / 2 : MP;
+      if (ok && (MP >= 64 || warp < 4)) {
+        tc_fence_after();
+        const int c_begin = MP >= 64 ? (warp >> 2) * kColsPerWarp : 0;
+#pragma unroll 1
+        for (int c0 = c_begin; c0 < c_begin + kColsPerWarp; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + C::kAccCol + (uint32_t)c0, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < c_begin + kColsPerWarp) red[(c0 + j) * kBN + row] = __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+      }
+      if (!conv_bar_and(ok)) {
+        ok = false;
+        break;  // uniform across the converter warps
+      }
+      if (t == 0) mbar_arrive(accempty);  // the MMA warp may overwrite the accumulator
+      if (!waited) {
+        griddep_wait();  // (already satisfied) orders this thread's reads/writes of y after the predecessor
+        waited = true;
+        if (peer) epoch = *reinterpret_cast<volatile uint32_t*>(po.count) + 1u;
+      }
+      const bool starts = useg % KB == 0;
+      const bool ends = (u0 + last + 1) % KB == 0;
+      if (!starts) {
+        // contributor: this CTA's partial of the tile into its workspace slot, then its flag. The
+        // barrier orders every thread's stores before thread 0's release (cumulative at GPU scope).
+        float4* dst = reinterpret_cast<float4*>(part + (int64_t)cta * MP * kBN);
+        const float4* srcv = reinterpret_cast<const float4*>(red);
+        for (int idx = t; idx < MP * kBN / 4; idx += 256) __stcg(dst + idx, srcv[idx]);
+        conv_bar_sync();
+        if (t == 0) st_release_u32(flags + cta, 1u);
+      } else {
+        if (!ends) {
+          // finisher: the following CTAs whose first segment lies in this tile each left a partial.
+          // Thread j polls contributor j's flag (all at once), then every thread adds, for its own
+          // elements, the partials in CTA order (fixed order: bit-reproducible).
+          const int64_t tile_end = (tile + 1) * KB;
+          int nc = 0;
+          while (cta + 1 + nc < G && ubeg(cta + 1 + nc) < tile_end) ++nc;
+          if (t == 0) s_ok = 1;
+          conv_bar_sync();
+          if (t < nc) {
+            uint32_t* f = flags + cta + 1 + t;
+            uint64_t t0 = 0;
+            for (uint32_t spin = 0; ld_acquire_u32(f) == 0u; ++spin) {
+              if ((spin & 31) == 31) {
+                const uint64_t now = global_ns();
+                if (t0 == 0) {
+                  t0 = now;
+                } else if (now - t0 > 1000000000ull) {
+                  mg_record_error(MG_ERR_TIMEOUT, 18);
+                  s_ok = 0;
+                  break;
+                }
+                __nanosleep(64);
+              }
+            }
+            *f = 0u;  // consumed (the next launch's writers run after this grid completed)
+          }
+          conv_bar_sync();
+          if (!s_ok) ok = false;
+          constexpr int kBatch = 8;  // partial loads in flight per thread
+          float4* acc4 = reinterpret_cast<float4*>(red);
+          for (int idx = t; idx < MP * kBN / 4; idx += 256) {
+            float4 acc = acc4[idx];
+            for (int j0 = 0; j0 < nc; j0 += kBatch) {
+              float4 v[kBatch];
+#pragma unroll
+              for (int j = 0; j < kBatch; ++j)
+                if (j0 + j < nc) v[j] = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)(cta + 1 + j0 + j) * MP * kBN) + idx);
+#pragma unroll
+              for (int j = 0; j < kBatch; ++j) {
+                if (j0 + j < nc) {
+                  acc.x += v[j].x;
+                  acc.y += v[j].y;
+                  acc.z += v[j].z;
+                  acc.w += v[j].w;
+                }
+              }
+            }
+            acc4[idx] = acc;
+          }
+          conv_bar_sync();
+        }
+        // epilogue of the whole tile from `red`: thread t takes weight row r0 and every second token
+        // column from `half` (SwiGLU: rows < 64 pair gate row r0 with up row r0 + 64)
+        const int64_t n0 = tile * kBN + r0;
+        const int64_t n1 = n0 + 64;
+        const bool active = swiglu ? ((t & 127) < 64 && n1 < N) : (n0 < N);
+        if (active) {
+          const float s0 = scales[n0];
+          const float b0 = bias ? bias[n0] : 0.f;
+          const float s1 = swiglu ? scales[n1] : 0.f;
+          const float b1 = (swiglu && bias) ? bias[n1] : 0.f;
+          const uint64_t tag = (uint64_t)epoch << 32;
+          for (int ml = half; ml < m_valid; ml += 2) {
+            const float a0 = red[ml * kBN + r0];
+            if (peer) {  // warp-uniform (N % 128 == 0): lane pairs (n, n+1) share one word
+              const float v = a0 * s0;
+              const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
+              if ((n0 & 1) == 0) {
+                const uint64_t word = tag | pack_bf16x2(v, v1);
+                const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + ((int64_t)ml * N + n0) / 2;
+                for (int r = 0; r < po.world; ++r) st_volatile_u64(po.recv[r] + off, word);
+              }
+            } else if (epi == MG_EPI_ADD_F32) {
+              red_add_f32(static_cast<float*>(y) + (int64_t)ml * ldy + n0, a0 * s0 + b0);
+            } else if (!swiglu) {
+              store_out(epi, y, (int64_t)ml * ldy + n0, a0 * s0 + b0);
+            } else {
+              const float gv = a0 * s0 + b0, uv = red[ml * kBN + r0 + 64] * s1 + b1;
+              static_cast<__nv_bfloat16*>(y)[(int64_t)ml * ldy + tile * 64 + r0] =
+                  __float2bfloat16_rn(silu_f(gv) * uv);
+            }
+          }
+        }
+      }
+      conv_bar_sync();  // `red` is free for the next segment
+      ++seg;
+    }
+    if (!waited) griddep_wait();
+  }
+  __syncthreads();
+  if (warp == kMmaWarp) {  // every accumulator has been drained
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+  // The last CTA to finish advances this rank's all-reduce count (read by the reduce kernel).
+  if (epi == MG_EPI_PEER_F32 && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(po.done, 1u) == gridDim.x - 1u) {
+      *reinterpret_cast<volatile uint32_t*>(po.done) = 0u;
+      *reinterpret_cast<volatile uint32_t*>(po.count) += 1u;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------------------
 int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
@@ -599,6 +995,52 @@ int dispatch_tc(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* 
   if (m <= 128) return MG_TC(128);
   return MG_TC(256);
 #undef MG_TC
+}
+
+// ---- stream-K dispatch (tile-packed codes, m <= 128) ----
+int sk_mp(int64_t m) { return m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : (m <= 128 ? 128 : 0))); }
+int sk_ctas_per_sm(int mp) { return mp <= 32 ? 2 : 1; }
+constexpr int64_t kSkMinUnits = 2;  // K blocks per CTA at least (fewer, bigger CTAs for small linears)
+size_t sk_flag_bytes(int64_t grid) { return (size_t)((grid * 4 + 255) / 256 * 256); }
+size_t sk_ws_bytes(int mp, int64_t grid) { return sk_flag_bytes(grid) + (size_t)grid * mp * kBN * 4; }
+
+template <int MP>
+int launch_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed, const float* scales,
+              const float* bias, int64_t n, void* y, int64_t ldy, int epi, void* ws, size_t ws_bytes,
+              cudaStream_t st, const PeerOut* po) {
+  using C = SkCfg<MP>;
+  static bool attr_done[64] = {};
+  static std::mutex attr_mu;
+  MG_CUDA_TRY(mg_once_per_device(attr_done, attr_mu, [] {
+    return cudaFuncSetAttribute(i8_gemm_sk<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  }));
+  const int64_t tiles = (n + kBN - 1) / kBN, kblocks = (k + kBK - 1) / kBK, units = tiles * kblocks;
+  int64_t grid = (int64_t)sm_count() * C::kCtasPerSm;
+  grid = std::min(grid, std::max<int64_t>(1, units / kSkMinUnits));
+  if (units * kBN > 0x7fffffff) return MG_ERR_UNSUPPORTED;
+  if (!ws || ws_bytes < sk_ws_bytes(MP, grid) || (reinterpret_cast<uintptr_t>(ws) & 255)) return MG_ERR_INVALID_ARG;
+  CUtensorMap mw, mx;
+  int rc = make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, kBK, (uint64_t)(units * kBN), kBK, kBK, kBN);
+  if (rc) return rc;
+  rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)k, (uint64_t)m, (uint64_t)ldx * 2, 64, MP);
+  if (rc) return rc;
+  uint32_t* flags = static_cast<uint32_t*>(ws);
+  float* part = reinterpret_cast<float*>(static_cast<char*>(ws) + sk_flag_bytes(grid));
+  MG_CUDA_TRY(mg_launch(i8_gemm_sk<MP>, dim3((unsigned)grid), dim3(kTcThreads), C::kSmemBytes, st, 1, mw, mx, (int)m,
+                        (int)k, n, scales, bias, y, ldy, epi, po ? *po : PeerOut{}, part, flags));
+  return MG_OK;
+}
+
+int dispatch_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed, const float* scales,
+                const float* bias, int64_t n, void* y, int64_t ldy, int epi, void* ws, size_t ws_bytes,
+                cudaStream_t st, const PeerOut* po = nullptr) {
+  switch (sk_mp(m)) {
+    case 16: return launch_sk<16>(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, ws, ws_bytes, st, po);
+    case 32: return launch_sk<32>(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, ws, ws_bytes, st, po);
+    case 64: return launch_sk<64>(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, ws, ws_bytes, st, po);
+    case 128: return launch_sk<128>(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, ws, ws_bytes, st, po);
+    default: return dispatch_tc(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, 0, st, true, po);
+  }
 }
 
 // [tiles][kblocks][128 rows][128 B]: packed[((t*KB + kb)*128 + r)*128 + c] = q[(t*128 + r)*k + kb*128 + c],
@@ -701,4 +1143,36 @@ extern "C" int mg_i8_linear_packed_rowpar(const void* x, int64_t m, int64_t k, i
   if (m == 0) return MG_OK;
   return dispatch_tc(x, m, k, ldx, packed, scales, nullptr, n, nullptr, n, MG_EPI_PEER_F32, split_k,
                      mg_stream(stream), true, &po);
+}
+
+// ---- stream-K entry points ----------------------------------------------------------------------
+extern "C" int64_t mg_i8_linear_sk_workspace_bytes(int64_t m) {
+  const int mp = sk_mp(m);
+  if (m <= 0 || !mp) return 0;
+  return (int64_t)sk_ws_bytes(mp, (int64_t)sm_count() * sk_ctas_per_sm(mp));
+}
+
+extern "C" int mg_i8_linear_packed_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                                      const float* scales, const float* bias, int64_t n, void* y, int64_t ldy,
+                                      int epi, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_linear_args(x, m, k, ldx, packed, scales, n, y, ldy, epi);
+  if (rc) return rc;
+  if (m == 0) return MG_OK;
+  return dispatch_sk(x, m, k, ldx, packed, scales, bias, n, y, ldy, epi, workspace, workspace_bytes,
+                     mg_stream(stream));
+}
+
+extern "C" int mg_i8_linear_packed_rowpar_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
+                                             const float* scales, int64_t n, void* comm, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+  PeerOut po;
+  int rc = mg_comm_peer_out(comm, &po);
+  if (rc) return rc;
+  if (m < 0 || k <= 0 || n <= 0 || !x || !packed || !scales || k % 16 || n % 128 || ldx < k || ldx % 8 ||
+      m * n > 2 * po.slot || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(packed)) & 15))
+    return MG_ERR_INVALID_ARG;
+  if (k > 0x7fffffff || m > 0x7fffffff) return MG_ERR_UNSUPPORTED;
+  if (m == 0) return MG_OK;
+  return dispatch_sk(x, m, k, ldx, packed, scales, nullptr, n, nullptr, n, MG_EPI_PEER_F32, workspace,
+                     workspace_bytes, mg_stream(stream), &po);
 }

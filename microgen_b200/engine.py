@@ -263,11 +263,17 @@ class DecodeEngine:
         self.logits = torch.zeros((B, spec.vocab), dtype=torch.float32, device=dev)
         ws = max(K.attn_workspace_bytes(b, self.hq, self.hkv, self.D, max_blocks_per_seq, ns)
                  for b in {1, max_batch} for ns in {0, max_blocks_per_seq})
-        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)  # tickets start at zero
         # pinned host staging for step inputs: tokens, positions, slots, ctx, then the table
         self.stage = torch.zeros(4 * B + B * max_blocks_per_seq, dtype=torch.int32, pin_memory=True)
         self.stage_np = self.stage.numpy()
         self.graphs: dict = {}
+        # MG_STREAMK=1 runs the linears on the stream-K kernel (one wave of CTAs, equal weight bytes each;
+        # it needs a zero-filled workspace for partial tiles); the default is the cluster split-K kernel,
+        # which measured faster in the decode step (A/B in the same run)
+        self.lin_ws = None
+        if isinstance(weights.lm_q, K.PackedWeight) and os.environ.get("MG_STREAMK", "0") == "1":
+            self.lin_ws = K.sk_workspace(max_batch, dev)
         # TP > 1: row-parallel linears push their partials straight into every rank's memory and a
         # fused reduce(+norm) kernel finishes the all-reduce (MG_FUSED_AR=0 falls back to NCCL).
         self.comm = None
@@ -328,7 +334,8 @@ class DecodeEngine:
                 with P("norm", b * H * 6):
                     self._norm(h, L.ln1_w, L.ln1_b, x)
             with P("i8_linear", self.linear_bytes(L.qkv_q, b, 4, nqkv)):
-                K.i8_linear(x, L.qkv_q, L.qkv_s, L.qkv_b, y=self.qkv[:b], epilogue=K.EPI_STORE_F32)
+                K.i8_linear(x, L.qkv_q, L.qkv_s, L.qkv_b, y=self.qkv[:b], epilogue=K.EPI_STORE_F32,
+                            workspace=self.lin_ws)
             with P("rope_kv_append", b * nqkv * 4 + b * self.hq * D * 4 + b * 2 * self.hkv * D * 2):
                 K.rope_kv_append(self.qkv[:b], self.positions[:b], self.cos_sin, self.slots[:b], self.hq,
                                  self.hkv, self.D, self.pool.k[l], self.pool.v[l], q_out=self.q[:b])
@@ -338,37 +345,40 @@ class DecodeEngine:
                                     validate=False)
             if fused:
                 with P("i8_linear", self.linear_bytes(L.o_q, b, 0, H) + push_bytes):
-                    K.i8_linear_rowpar(self.attn[:b], L.o_q, L.o_s, self.comm)
+                    K.i8_linear_rowpar(self.attn[:b], L.o_q, L.o_s, self.comm, workspace=self.lin_ws)
                 with P("rowpar_reduce", push_bytes + b * H * 10):
                     K.rowpar_reduce_norm(self.comm, h, L.o_b, norm_kind, L.ln2_w, L.ln2_b, s.eps, x)
             else:
                 bias_o = L.o_b if self.rank == 0 else None
                 with P("i8_linear", self.linear_bytes(L.o_q, b, 8, H)):
                     row_parallel_residual(h, lambda y, e: K.i8_linear(self.attn[:b], L.o_q, L.o_s, bias_o, y=y,
-                                                                      epilogue=e), self.rank, self.world, self.group)
+                                                                      epilogue=e, workspace=self.lin_ws),
+                                          self.rank, self.world, self.group)
                 with P("norm", b * H * 6):
                     self._norm(h, L.ln2_w, L.ln2_b, x)
             epi_mlp = K.EPI_GELU_BF16 if s.family == "gpt2" else K.EPI_SWIGLU_BF16
             with P("i8_linear", self.linear_bytes(L.gu_q, b, 2, self.act.shape[1])):
-                K.i8_linear(x, L.gu_q, L.gu_s, L.gu_b, y=self.act[:b], epilogue=epi_mlp)
+                K.i8_linear(x, L.gu_q, L.gu_s, L.gu_b, y=self.act[:b], epilogue=epi_mlp, workspace=self.lin_ws)
             if fused:
                 nxt_w, nxt_b = ((w.layers[l + 1].ln1_w, w.layers[l + 1].ln1_b) if l + 1 < len(w.layers)
                                 else (w.norm_w, w.norm_b))
                 with P("i8_linear", self.linear_bytes(L.d_q, b, 0, H) + push_bytes):
-                    K.i8_linear_rowpar(self.act[:b], L.d_q, L.d_s, self.comm)
+                    K.i8_linear_rowpar(self.act[:b], L.d_q, L.d_s, self.comm, workspace=self.lin_ws)
                 with P("rowpar_reduce", push_bytes + b * H * 10):
                     K.rowpar_reduce_norm(self.comm, h, L.d_b, norm_kind, nxt_w, nxt_b, s.eps, x)
             else:
                 bias_d = L.d_b if self.rank == 0 else None
                 with P("i8_linear", self.linear_bytes(L.d_q, b, 8, H)):
                     row_parallel_residual(h, lambda y, e: K.i8_linear(self.act[:b], L.d_q, L.d_s, bias_d, y=y,
-                                                                      epilogue=e), self.rank, self.world, self.group)
+                                                                      epilogue=e, workspace=self.lin_ws),
+                                          self.rank, self.world, self.group)
         if compute_logits:
             if not fused:
                 with P("norm", b * H * 6):
                     self._norm(h, w.norm_w, w.norm_b, x)
             with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, s.vocab)):
-                K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32)
+                K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32,
+                            workspace=self.lin_ws)
             with P("argmax", b * s.vocab * 4):
                 K.argmax_rows(self.logits[:b], out=self.next_tokens[:b])
 

@@ -103,11 +103,29 @@ def _linear_args(x, q, scales, bias, y, epilogue):
     return m, k, n, y
 
 
-def i8_linear(x, q, scales, bias=None, y=None, epilogue=EPI_STORE_BF16, algo: str = "auto", split_k: int = 0):
+def sk_workspace_bytes(m: int) -> int:
+    """Workspace bytes of the stream-K linear for m tokens (0 when m > 128: that path is not used)."""
+    return int(_lib.load().mg_i8_linear_sk_workspace_bytes(int(m)))
+
+
+def sk_workspace(max_m: int, device) -> torch.Tensor | None:
+    """A zero-filled workspace that serves every stream-K linear call with m <= max_m on ``device``."""
+    need = max([sk_workspace_bytes(m) for m in (1, 17, 33, 65) if m <= max_m] or [0])
+    return torch.zeros(need, dtype=torch.uint8, device=device) if need else None
+
+
+def i8_linear(x, q, scales, bias=None, y=None, epilogue=EPI_STORE_BF16, algo: str = "auto", split_k: int = 0,
+              workspace=None):
     """y = epilogue(x · (q·s)ᵀ + bias); returns y. algo: "auto" | "tc" | "simt" (row-major q);
-    a PackedWeight q runs the tensor-core kernel on tile-packed codes."""
+    a PackedWeight q runs the tensor-core kernel on tile-packed codes: the stream-K form when a zero-filled
+    ``workspace`` (``sk_workspace``) is given, else the cluster split-K form (``split_k``)."""
     m, k, n, y = _linear_args(x, q, scales, bias, y, epilogue)
     if isinstance(q, PackedWeight):
+        if workspace is not None:
+            _lib.call("mg_i8_linear_packed_sk", _ptr(x), m, k, x.stride(0), _ptr(q.data), _ptr(scales), _ptr(bias),
+                      n, _ptr(y), y.stride(0), int(epilogue), _ptr(workspace),
+                      workspace.numel() * workspace.element_size(), _stream())
+            return y
         _lib.call("mg_i8_linear_packed", _ptr(x), m, k, x.stride(0), _ptr(q.data), _ptr(scales), _ptr(bias), n,
                   _ptr(y), y.stride(0), int(epilogue), int(split_k), _stream())
         return y
@@ -147,7 +165,8 @@ def attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks=0) -> int:
 def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared_blocks=0, out=None,
                       workspace=None, validate=True):
     """q fp32 [b, hq, d]; pools bf16 [nblk, hkv, 16, d]; tables int32 [b, max_blocks]; ctx int32 [b].
-    Returns bf16 [b, hq*d].
+    Returns bf16 [b, hq*d]. ``workspace`` (optional; allocated when missing) must be zero-filled before its
+    first use: the kernel's merge tickets live in it and every launch leaves them at zero.
 
     With ``n_shared_blocks`` > 0 the first that many entries of every table must equal row 0's (the
     kernel reads the shared blocks once, from row 0); ``validate`` checks this before the launch and raises
@@ -167,14 +186,12 @@ def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared
         check_shared_prefix(block_tables[:, :n_shared_blocks].cpu().numpy(), n_shared_blocks)
     ws = attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks)
     if ws and (workspace is None or workspace.numel() * workspace.element_size() < ws):
-        workspace = torch.empty(ws, dtype=torch.uint8, device=q.device)
+        workspace = torch.zeros(ws, dtype=torch.uint8, device=q.device)
     if out is None:
         out = torch.empty((b, hq * d), dtype=torch.bfloat16, device=q.device)
     _lib.call("mg_paged_decode_attn", _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables),
               max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks, float(scale), _ptr(out),
               _ptr(workspace if ws else None), ws, _stream())
-    if ws:
-        _lib.LAUNCHES[0] += 1  # the split-combine kernel
     return out
 
 
@@ -268,8 +285,9 @@ class Comm:
             self._h = C.c_void_p()
 
 
-def i8_linear_rowpar(x, q: PackedWeight, scales, comm: Comm, split_k: int = 0) -> None:
-    """This rank's partial x · (q·s)ᵀ, pushed into every rank's receive slot (no bias)."""
+def i8_linear_rowpar(x, q: PackedWeight, scales, comm: Comm, split_k: int = 0, workspace=None) -> None:
+    """This rank's partial x · (q·s)ᵀ, pushed into every rank's receive slot (no bias); with a stream-K
+    ``workspace`` the stream-K kernel computes it."""
     _need(x, torch.bfloat16, "x", contiguous=False)
     _need(scales, torch.float32, "scales")
     if not isinstance(q, PackedWeight):
@@ -277,6 +295,10 @@ def i8_linear_rowpar(x, q: PackedWeight, scales, comm: Comm, split_k: int = 0) -
     n, k = q.shape
     if x.dim() != 2 or x.stride(1) != 1 or x.shape[1] != k:
         raise ValueError("x must be [m, k] with unit inner stride")
+    if workspace is not None:
+        _lib.call("mg_i8_linear_packed_rowpar_sk", _ptr(x), x.shape[0], k, x.stride(0), _ptr(q.data), _ptr(scales),
+                  n, comm.handle, _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
+        return
     _lib.call("mg_i8_linear_packed_rowpar", _ptr(x), x.shape[0], k, x.stride(0), _ptr(q.data), _ptr(scales), n,
               comm.handle, int(split_k), _stream())
 

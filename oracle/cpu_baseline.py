@@ -117,3 +117,35 @@ def measure(hidden, heads, kv_heads, head_dim, inter, vocab, layers, batch, ctx,
         "setup_s": start - t_setup,
         "threads": os.cpu_count() or 1,
     }
+
+
+def measure_steps(hidden, heads, kv_heads, head_dim, inter, vocab, layers, batch, ctx, budget_s=60.0,
+                  max_steps=20, warmup=1, eps=1e-5, theta=500000.0) -> dict:
+    """Time WHOLE decode steps of the CPU port: each step runs the decoder layer ``layers`` times (one
+    layer's weights and cache, applied once per layer of the model: the same arithmetic and the same
+    bytes streamed as ``layers`` distinct layers) and then the final norm + lm_head + argmax. Runs
+    ``warmup`` untimed steps, then timed steps until ``budget_s`` is spent (at least one, at most
+    ``max_steps``); returns the number of steps actually timed with the mean step time."""
+    layer = LlamaLayerPort(hidden, heads, kv_heads, head_dim, inter, batch, ctx, eps, theta)
+    rng = np.random.default_rng(1)
+    head = _rand_codes(rng, vocab, hidden)
+    h0 = rng.standard_normal((batch, hidden), dtype=np.float32)
+
+    def step():
+        h = h0
+        for _ in range(layers):
+            h = layer.step(h)
+        logits = _rms(h, np.ones(hidden, np.float32), eps) @ _deq(*head).T
+        return np.argmax(logits, axis=-1)
+
+    for _ in range(warmup):
+        step()
+    times = []
+    start = time.perf_counter()
+    while not times or (len(times) < max_steps and time.perf_counter() - start < budget_s):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    step_s = sum(times) / len(times)
+    return {"tokens_per_s": batch / step_s, "step_s": step_s, "steps": len(times), "warmup": warmup,
+            "timed_s": sum(times), "threads": os.cpu_count() or 1}
