@@ -87,14 +87,33 @@ def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps:
         for x, q, sc, bias, y, e, _ in lin:
             K.i8_linear(x, q, sc, bias, y=y, epilogue=e, workspace=eng.lin_ws)
 
+    families = [("i8_linear", run_lin, len(lin), sum(t[-1] for t in lin))]
+    if eng.block_args is not None:
+        # the step's persistent layer launches (every linear, norm and RoPE/KV append of the layers), and
+        # the lm_head linear on its own
+        def run_block():
+            for a in eng.block_args:
+                a.m = b
+                K.decode_block(a, eng.block_ws, eng.comm)
+
+        head = lin[-1]
+
+        def run_head():
+            x, q, sc, bias, y, e, _ = head
+            K.i8_linear(x, q, sc, bias, y=y, epilogue=e)
+
+        nb = len(eng.block_args)
+        families = [("decode_block", run_block, nb, sum(eng.block_bytes(i, b) for i in range(nb))),
+                    ("lm_head", run_head, 1, head[-1])]
+
     def run_attn():
         for l in range(len(w.layers)):
             K.paged_decode_attn(eng.q[:b], eng.pool.k[l], eng.pool.v[l], tab, ctx, eng.scale,
                                 n_shared_blocks=n_shared_blocks, out=eng.attn[:b], workspace=eng.workspace)
 
     out = {}
-    for name, fn, n, nbytes in (("i8_linear", run_lin, len(lin), sum(t[-1] for t in lin)),
-                                ("paged_attn", run_attn, len(w.layers), attn_bytes * len(w.layers))):
+    families.append(("paged_attn", run_attn, len(w.layers), attn_bytes * len(w.layers)))
+    for name, fn, n, nbytes in families:
         fn()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -709,8 +728,11 @@ def main():
         "vs_baseline": None, "dtype": "int8 weights x bf16 activations, fp32 accumulate", "data": "synthetic",
         "config": workload_config(args.workload, wl, world),
         "setup": {"l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True,
-                  "row_parallel_reduce": reduce_kind, "linear_kernel": "stream-K" if eng.lin_ws is not None
-                  else "cluster split-K", "timed_window_mean_ctx": round(mean_pos + 1)},
+                  "row_parallel_reduce": reduce_kind,
+                  "linear_kernel": ("persistent layer kernel (decode_block) + cluster split-K lm_head"
+                                    if eng.block_args is not None else
+                                    "stream-K" if eng.lin_ws is not None else "cluster split-K"),
+                  "timed_window_mean_ctx": round(mean_pos + 1)},
         "roofline": roofline, "step_roofline": step_roofline, "kernel_chains": chains, "nvlink": nvlink,
         "kernels": kernels,
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst,

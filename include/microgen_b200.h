@@ -122,6 +122,75 @@ int mg_i8_linear_packed_rowpar_sk(const void* x, int64_t m, int64_t k, int64_t l
                                   const float* scales, int64_t n, void* comm, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* ---- persistent decode layer: every linear, norm and the RoPE/KV append between two attentions -----
+ * One launch replaces, for one layer boundary of a decode step (M <= 32 tokens):
+ *   quantized.py:24-27 QuantizedLinear.forward of o_proj, gate/up, down_proj, q/k/v (tile-packed codes),
+ *   parallel.py:40-81 RowParallelLinear + its all-reduce for o_proj and down_proj (comm != NULL),
+ *   the HF post-attention norm, SwiGLU (modeling_llama.py:182-183) or GELU MLP, the next input norm, and
+ *   kv_cache.py:76-127 KVCacheState.update with RoPE (one paged slot write per token).
+ * Phases (flags): MG_BLK_O      h += attn · Woᵀ (+ bias)                       [attn bf16 m x hq*d]
+ *                 MG_BLK_MLP    x2 = norm2(h); act = mlp(x2 · Wguᵀ); h += act · Wdᵀ (+ bias)
+ *                 MG_BLK_N1     x1 = norm1(h)  (the next layer's input norm, or the final norm)
+ *                 MG_BLK_QKV    q_out, K/V slots = rope(x1 · Wqkvᵀ + b)
+ * Enabled phases run in that order; a phase whose producer phase is not enabled reads its input as it
+ * was before the launch. norm: MG_NORM_RMS (w) or MG_NORM_LAYER (w, b). mlp: MG_EPI_SWIGLU_BF16 (gate/up
+ * rows interleaved in 64-row groups) or MG_EPI_GELU_BF16. o.n = down.n = hidden and gate_up.n are
+ * multiples of 128; qkv.n = (hq + 2*hkv) * head_dim (any multiple of 16: the packed codes are zero-padded
+ * to whole tiles); every k a multiple of 16; head_dim in {32, 64, 128}; cos_sin NULL = no RoPE (GPT-2).
+ * comm (world > 1, from mg_comm_create/open): o and down are this rank's row-parallel shards; their
+ * tiles are pushed to every rank and the norm sums them in rank order (bias once), as
+ * mg_i8_linear_packed_rowpar + mg_rowpar_reduce_norm do; NULL = world 1.
+ * workspace: mg_decode_block_workspace_bytes() bytes, 256-byte aligned, zero-filled before its first use.
+ * Its first 64 KB are control words (tile tickets, flags, phase counters) that every launch leaves at zero;
+ * the split partials follow. So one workspace serves any stream-ordered sequence of launches whose plans
+ * fit in it, the different plans of a model's layer boundaries included. One CTA per SM; the launch assumes the whole GPU (a CTA that cannot
+ * become resident makes the others' bounded waits give up with MG_ERR_TIMEOUT). */
+#define MG_NORM_RMS 1
+#define MG_NORM_LAYER 2
+#define MG_BLK_O 1
+#define MG_BLK_MLP 2
+#define MG_BLK_N1 4
+#define MG_BLK_QKV 8
+typedef struct mg_block_linear {
+  const int8_t* packed; /* tile-packed codes of [n, k] (mg_i8_pack_weights) */
+  const float* scales;  /* [n] */
+  const float* bias;    /* [n] or NULL */
+  int64_t n, k;
+} mg_block_linear;
+typedef struct mg_block_args {
+  int m, flags, hidden, hq, hkv, head_dim, norm, mlp;
+  float eps;
+  int max_pos;
+  mg_block_linear o, gate_up, down, qkv;
+  float* h;                         /* fp32 [m, hidden] residual stream, updated in place */
+  const void* attn;                 /* bf16 [m, hq*head_dim]: the o_proj input */
+  const float* n2_w; const float* n2_b;
+  void* x2;                         /* bf16 [m, hidden]: norm2 output */
+  void* act;                        /* bf16 [m, down.k]: MLP activation */
+  const float* n1_w; const float* n1_b;
+  void* x1;                         /* bf16 [m, hidden]: norm1 output (QKV input, or lm_head input) */
+  const float* cos_sin;             /* fp32 [max_pos, head_dim] (cos | sin) or NULL */
+  const int32_t* positions;         /* [m] */
+  const int32_t* slots;             /* [m] paged slot of the new token */
+  float* q_out;                     /* fp32 [m, hq, head_dim] */
+  void* k_pool; void* v_pool;       /* bf16 [num_blocks, hkv, 16, head_dim] of the QKV phase's layer */
+  int64_t num_blocks;
+} mg_block_args;
+int mg_decode_block_workspace_bytes(const mg_block_args* args, size_t* bytes);
+int mg_decode_block(const mg_block_args* args, void* comm, void* workspace, size_t workspace_bytes, void* stream);
+/* Diagnosis of the first bounded wait of mg_decode_block that gave up on the current device (MG_ERR_TIMEOUT
+ * in the device error word): out[0] = site (0 = none), [1] CTA, [2] thread, [3..4] site-specific words,
+ * [8..15] the launch's first eight control words; out[32 + 4*c + r]: the
+ * progress of CTA c < 256 in role r (0 producer, 1 converters, 2 MMA, 3 epilogue) when that wait gave
+ * up. out holds 32 + 1024 words. Synchronous; clear != 0 resets the first 32. */
+int mg_decode_block_diag(uint32_t* out32, int clear);
+/* Timeline of the latest mg_decode_block launch on the current device: out[16*c + k] = globaltimer (ns)
+ * of CTA c (< ctas <= 256) at point k — 0 entry, 1 dependency released, 2..5 first activation tile of
+ * o_proj / gate-up / down / QKV requested, 6 last MMA issued, 7 epilogue start, 8 o_proj drained,
+ * 9 norm2 done, 10 gate/up drained, 11 down drained, 12 norm1 done, 13 QKV drained, 14 last weight
+ * tile converted, 15 exit. Points a launch does not reach keep older values. Synchronous. */
+int mg_decode_block_trace(uint64_t* out, int ctas);
+
 /* ---- paged KV: RoPE + append (kv_cache.py:76-127, as one slot write per token) ------------ */
 /* qkv fp32 [b, (hq+2*hkv)*d] (row stride ld_qkv): q heads, then k heads, then v heads.
  * rope: cos_sin fp32 [max_pos, d] (cos of the d/2 frequencies, then sin), NULL = no rotation.
@@ -138,11 +207,8 @@ int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t* positions
  * n_shared_blocks: the first n_shared_blocks entries of every table are the same blocks
  * (a shared prefix); they are read once per batch. 0 = no sharing. A table whose leading entries differ
  * from row 0's is recorded as MG_ERR_DEVICE (site 403).
- * workspace: device scratch of mg_paged_attn_workspace_bytes() bytes, 16-byte aligned (may be NULL if 0),
- * zero-filled before its first use: its first 64 KB hold one merge ticket per (sequence, kv head), which the
- * last CTA of the pair resets, so every launch leaves the tickets at zero and one workspace (large enough)
- * serves launches of any shape; the split partials follow. b * hkv <= 16384 (else MG_ERR_UNSUPPORTED).
- * One launch (no separate combine kernel) covers the whole attention. */
+ * workspace: device scratch of mg_paged_attn_workspace_bytes() bytes (may be NULL if 0). When the launch
+ * splits a sequence's blocks over several CTAs, a second kernel merges the split partials (log-sum-exp). */
 int mg_paged_attn_workspace_bytes(int b, int hq, int hkv, int d, int max_blocks, int n_shared_blocks,
                                   size_t* bytes);
 int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
@@ -162,10 +228,9 @@ int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool,
  * make that first call before any stream capture. The address is kept for the life of the process:
  * after cudaDeviceReset (which unloads the library's device code) this entry point must not be called
  * again on that device. All calls share the array: calls whose kernels overlap on the GPU (e.g. on two
- * streams) race on it — serialise them. Nothing in it needs clearing: each call writes every split slot
- * it later reads (a split whose bounded wait gave up writes an empty softmax state and records
- * MG_ERR_TIMEOUT), and the merge tickets, zero when the library loads, are left at zero by every call
- * (every CTA counts itself in, on the error paths too). */
+ * streams) race on it — serialise them. Nothing in it needs clearing: each call writes every slot it
+ * later reads (a split whose bounded wait gave up writes an empty softmax state and records
+ * MG_ERR_TIMEOUT). */
 #define MG_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
 int mg_paged_decode_attn_noalloc(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
                                  const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,

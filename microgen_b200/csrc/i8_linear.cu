@@ -403,10 +403,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       uint4 v[4];
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) v[c4] = *reinterpret_cast<const uint4*>(src + (((hh * 4 + c4) ^ (row & 7)) << 4));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&wempty[s]);  // the bytes are in registers: the stage can refill
-      if (i >= NA) ok = mbar_wait(&aempty[ab], ((i / NA) - 1) & 1, 5);
-      if (!ok) break;
       uint32_t r[32];
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
@@ -415,6 +411,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         i8x4_to_bf16x4(v[c4].z, r[c4 * 8 + 4], r[c4 * 8 + 5]);
         i8x4_to_bf16x4(v[c4].w, r[c4 * 8 + 6], r[c4 * 8 + 7]);
       }
+      // the bytes have been consumed (converted): the stage can refill. Releasing it right after the shared
+      // loads were issued could let the next TMA write land before a load returned.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[s]);
+      if (i >= NA) ok = mbar_wait(&aempty[ab], ((i / NA) - 1) & 1, 5);
+      if (!ok) break;
       tmem_st32(tmem + lane_base + (uint32_t)(ab * 64 + hh * 32), r);
       tc_wait_st();
       tc_fence_before();
@@ -757,18 +759,15 @@ __global__ void __launch_bounds__(kTcThreads, SkCfg<MP>::kCtasPerSm)
       for (; i <= last; ++i) {
         const int s = i % SW, ab = i % NA;
         if (ok) ok = mbar_wait(&wfull[s], (i / SW) & 1, 15);
+        // the TMEM buffer is claimed before the stage is read, so no converted registers stay live across a wait
+        if (ok && i >= NA) ok = mbar_wait(&aempty[ab], ((i / NA) - 1) & 1, 16);
         uint4 v[4];
+        uint32_t r[32];
         if (ok) {
           const uint8_t* src = smem + s * kWStageBytes + row * 128;
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4)
             v[c4] = *reinterpret_cast<const uint4*>(src + (((hh * 4 + c4) ^ (row & 7)) << 4));
-        }
-        __syncwarp();
-        if (ok && lane == 0) mbar_arrive(&wempty[s]);
-        if (ok && i >= NA) ok = mbar_wait(&aempty[ab], ((i / NA) - 1) & 1, 16);
-        if (ok) {
-          uint32_t r[32];
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
             i8x4_to_bf16x4(v[c4].x, r[c4 * 8 + 0], r[c4 * 8 + 1]);
@@ -776,6 +775,11 @@ __global__ void __launch_bounds__(kTcThreads, SkCfg<MP>::kCtasPerSm)
             i8x4_to_bf16x4(v[c4].z, r[c4 * 8 + 4], r[c4 * 8 + 5]);
             i8x4_to_bf16x4(v[c4].w, r[c4 * 8 + 6], r[c4 * 8 + 7]);
           }
+        }
+        // released only after the bytes were consumed (converted), see the cluster kernel's converters
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&wempty[s]);
+        if (ok) {
           tmem_st32(tmem + lane_base + (uint32_t)(ab * 64 + hh * 32), r);
           tc_wait_st();
           tc_fence_before();

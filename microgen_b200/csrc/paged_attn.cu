@@ -8,21 +8,17 @@
 // A CTA is one producer warp (TMA loads of (K, V) tiles into a ring of kStages shared-memory
 // stages, 128-byte swizzled so the ldmatrix reads are conflict-free) and kCons consumer warps.
 // One launch covers two kinds of CTAs:
-//   * shared CTAs — one per (kv head, chunk of shared-prefix blocks, group of kCons query row
-//     tiles). Each block of the chunk is loaded once and every sequence's query group is run
+//   * shared CTAs — one per (kv head, chunk of up to kChunk shared-prefix blocks, group of
+//     kCons query row tiles). The chunk is loaded once and every sequence's query group is run
 //     against it (rows = batch x group), so a prefix shared by the whole batch is read from HBM
-//     once per batch (and row group) instead of once per sequence.
+//     once per batch instead of once per sequence.
 //   * private CTAs — one per (sequence, kv head, split) over the sequence's own blocks. Tile i
 //     of the split goes to stage i % kStages and consumer warp i % kCons (each warp owns
 //     kStages/kCons stages, so that many of its tiles are in flight); each warp keeps its own
 //     online-softmax state, merged at the end.
-// Chunks and splits hold about the same number of blocks (about two waves of CTAs in all). Each
-// CTA leaves (m, l, unnormalised O) per query head in a workspace slot and counts itself in on a
-// per-(sequence, kv head) ticket; the last contributor merges the slots (log-sum-exp) into the
-// output and resets the ticket, so no second kernel runs. With no shared prefix and one split the
-// private CTA writes the normalised output itself.
-#include <algorithm>
-
+// Each CTA leaves (m, l, unnormalised O) per query head in a workspace slot, and a combine
+// kernel merges the slots (log-sum-exp). With no shared prefix and one split the private CTA
+// writes the normalised output itself.
 #include "common.cuh"
 
 namespace {
@@ -31,7 +27,8 @@ constexpr int kCons = 4;                 // consumer warps
 constexpr int kProd = kCons;             // producer warp index
 constexpr int kThreads = (kCons + 1) * 32;
 constexpr int kStages = 8;               // KV ring stages (a multiple of kCons)
-static_assert(kStages % kCons == 0, "ring layout");
+constexpr int kChunk = 8;                // shared-prefix blocks per shared CTA (<= kStages)
+static_assert(kStages % kCons == 0 && kChunk <= kStages, "ring layout");
 
 template <int D>
 struct AttnCfg {
@@ -272,104 +269,21 @@ struct AttnParams {
   int max_blocks;
   const int32_t* ctx;
   int b, hq, hkv, group;
-  int n_shared;      // shared-prefix blocks
-  int chunk;         // shared-prefix blocks per shared CTA
-  int n_chunks;      // shared CTAs per (kv head, row group)
+  int n_shared;   // shared-prefix blocks
+  int n_shared_ctas_per_head;
   int n_row_groups;  // shared CTAs per (kv head, chunk): groups of kCons query row tiles
-  int nsplit, bps;   // private splits and blocks per split
-  int nslots;        // workspace slots per (seq, head) = n_chunks + nsplit
+  int nsplit, bps;  // private splits and blocks per split
+  int nslots;       // workspace slots per (seq, head) = shared chunks + nsplit
   float qscale;
   __nv_bfloat16* out;
-  float* ws_o;        // [b, hq, nslots, d]
-  float* ws_ml;       // [b, hq, nslots, 2]
-  uint32_t* tickets;  // [b, hkv]: contributors of (seq, kv head) that have written their slots
-  bool direct;        // one slot: the private CTA writes the final output
+  float* ws_o;  // [b, hq, nslots, d]
+  float* ws_ml; // [b, hq, nslots, 2]
+  bool direct;  // private CTA writes the final output
 };
-
-constexpr int kRowsPerGroup = kCons * 16;  // query rows (seq, head) per shared CTA
-
-// Contributors to the slots of (seq, kv head): every private split, and for each shared chunk the shared
-// CTAs whose row group holds one of the sequence's query rows.
-__device__ __forceinline__ int expected_contributors(const AttnParams& p, int seq) {
-  if (p.n_chunks == 0) return p.nsplit;
-  const int lo = seq * p.group / kRowsPerGroup, hi = ((seq + 1) * p.group - 1) / kRowsPerGroup;
-  return p.nsplit + p.n_chunks * (hi - lo + 1);
-}
-
-// All threads of the CTA, after the CTA wrote its slots of (seq, kv head h): count the CTA in; the last of
-// the pair's contributors merges the pair's slots into the bf16 output and resets the ticket for the next
-// launch. Thread 0 counts with an acquire-release atomic after a CTA barrier, which publishes every
-// thread's slot writes (and, for the last contributor, makes every other contributor's visible); the
-// merging CTA reads the slots from L2. The merge stages each slot's (m, l) in shared memory `scratch`
-// (2 x group x nslots floats), turns them into one weight per (head, slot) — exp2(m - M) / L — and then
-// sums the weighted O slots with float4 loads issued kBatch at a time.
-template <int D>
-__device__ void arrive_and_merge(const AttnParams& p, int seq, int h, int* s_last, float* scratch) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t* tk = p.tickets + (int64_t)seq * p.hkv + h;
-    uint32_t prev;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(tk) : "memory");
-    const bool last = prev + 1u == (uint32_t)expected_contributors(p, seq);
-    if (last) *tk = 0u;  // every contributor of this launch has counted itself
-    *s_last = last;
-  }
-  __syncthreads();
-  if (!*s_last) return;
-  const int G = p.group, S = p.nslots;
-  const int64_t row0 = ((int64_t)seq * p.hq + (int64_t)h * G) * S;  // slot index of (head h*G, slot 0)
-  float* wm = scratch;          // [G][S] m, then the weights
-  float* wl = scratch + G * S;  // [G][S] l
-  for (int i = threadIdx.x; i < G * S; i += kThreads) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml) + row0 + i);
-    wm[i] = ml.x;
-    wl[i] = ml.y;
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    float* m = wm + threadIdx.x * S;
-    const float* l = wl + threadIdx.x * S;
-    float M = -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, m[s]);
-    float L = 0.f;
-    for (int s = 0; s < S; ++s) L += M == -INFINITY ? 0.f : l[s] * exp2f(m[s] - M);
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    for (int s = 0; s < S; ++s) m[s] = M == -INFINITY ? 0.f : exp2f(m[s] - M) * inv;
-  }
-  __syncthreads();
-  constexpr int kBatch = 8;
-  for (int e = threadIdx.x; e < G * (D / 4); e += kThreads) {
-    const int row = e / (D / 4), d4 = e % (D / 4);
-    const float* w = wm + row * S;
-    const float4* src = reinterpret_cast<const float4*>(p.ws_o + (row0 + (int64_t)row * S) * D) + d4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < S; s0 += kBatch) {
-      float4 v[kBatch];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j)
-        if (s0 + j < S) v[j] = __ldcg(src + (int64_t)(s0 + j) * (D / 4));
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (s0 + j < S) {
-          const float wj = w[s0 + j];
-          acc.x = fmaf(v[j].x, wj, acc.x);
-          acc.y = fmaf(v[j].y, wj, acc.y);
-          acc.z = fmaf(v[j].z, wj, acc.z);
-          acc.w = fmaf(v[j].w, wj, acc.w);
-        }
-      }
-    }
-    uint2 u;
-    u.x = pack_bf16x2(acc.x, acc.y);
-    u.y = pack_bf16x2(acc.z, acc.w);
-    *reinterpret_cast<uint2*>(p.out + ((int64_t)seq * p.hq + h * G + row) * D + d4 * 4) = u;
-  }
-  __syncthreads();  // `scratch` may be reused by the caller's next merge
-}
 
 template <int D, bool T>
 __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, int pair, int sp,
-                            uint8_t* smem, uint64_t* full, uint64_t* empty, int* s_last) {
+                            uint8_t* smem, uint64_t* full, uint64_t* empty) {
   using C = AttnCfg<D>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = pair / p.hkv, h = pair % p.hkv;
@@ -492,7 +406,7 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
     if (p.direct) {
       p.out[((int64_t)seq * p.hq + head) * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
     } else {
-      const int slot = p.n_chunks + sp;
+      const int slot = p.n_shared_ctas_per_head + sp;
       const int64_t base = ((int64_t)seq * p.hq + head) * p.nslots + slot;
       p.ws_o[base * D + d] = O;
       if (d == 0) {
@@ -501,90 +415,67 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
       }
     }
   }
-  if (!p.direct) arrive_and_merge<D>(p, seq, h, s_last, reinterpret_cast<float*>(smem));
 }
 
-// Shared-prefix CTA (kv head h, chunk of p.chunk shared blocks, row group rg): each block is loaded once
-// into the ring and every active consumer warp (one 16-row query tile each, rows = (sequence, head in
-// the group)) runs its tile against it; a stage is refilled once all active consumers released it.
 template <int D>
 __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, int h, int chunk,
-                           int rg, uint8_t* smem, uint64_t* full, uint64_t* empty, int* s_last) {
+                           int rg, uint8_t* smem, uint64_t* full) {
   using C = AttnCfg<D>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int blk0 = chunk * p.chunk;
-  const int nb = max(0, min(p.chunk, p.n_shared - blk0));
-  const int rows = p.b * p.group;
+  const int blk0 = chunk * kChunk;
+  const int nb = min(kChunk, p.n_shared - blk0);
+  // shared blocks are the first n_shared entries of every table; read them from sequence 0's table
   if (warp == kProd) {
-    // shared blocks are the first n_shared entries of every table; read them from sequence 0's table
-    auto entry = [&](int i) { return i < nb ? p.tables[blk0 + i] : 0; };
-    int cur = entry(lane), nxt = entry(32 + lane);
-    bool ok = true;
-    for (int i = 0; i < nb && ok; ++i) {
-      if (i > 0 && (i & 31) == 0) {
-        cur = nxt;
-        nxt = entry(i + 32 + lane);
-      }
-      int64_t phys = __shfl_sync(0xffffffffu, cur, i & 31);
-      if (phys < 0 || phys >= p.num_blocks) {
-        if (lane == 0) mg_record_error(MG_ERR_DEVICE, 402);
-        phys = 0;
-      }
-      if (lane == 0) {
-        const int s = i % kStages;
-        if (i >= kStages) ok = mbar_wait(&empty[s], ((i / kStages) - 1) & 1, 413);
-        if (ok) load_stage<D>(smem + s * C::kStageBytes, tk, tv, &full[s], (int)((phys * p.hkv + h) * 16));
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+    int64_t phys = lane < nb ? p.tables[blk0 + lane] : 0;
+    if (phys < 0 || phys >= p.num_blocks) {
+      mg_record_error(MG_ERR_DEVICE, 402);
+      phys = 0;
     }
-  } else {
-    const int t = rg * kCons + warp;  // this warp's 16-row query tile
-    if (t * 16 < rows) {
-      const int c = (lane & 3) * 2;
-      const int r0 = t * 16 + (lane >> 2), r1 = r0 + 8;
-      const int s0 = r0 < rows ? r0 / p.group : -1, s1 = r1 < rows ? r1 / p.group : -1;
-      uint32_t qa[D / 16][4];
-      load_q<D>(qa, p.q, p.hq, s0, h * p.group + (r0 % p.group), s1, h * p.group + (r1 % p.group), p.qscale, lane);
-      float o[D / 8][4];
+    for (int i = 0; i < nb; ++i) {
+      const int64_t ph = __shfl_sync(0xffffffffu, phys, i);
+      if (lane == 0) load_stage<D>(smem + i * C::kStageBytes, tk, tv, &full[i], (int)((ph * p.hkv + h) * 16));
+    }
+    return;
+  }
+  const int rows = p.b * p.group;
+  const int t = rg * kCons + warp;  // this warp's 16-row query tile
+  if (t * 16 >= rows) return;
+  const int c = (lane & 3) * 2;
+  const int r0 = t * 16 + (lane >> 2), r1 = r0 + 8;
+  const int s0 = r0 < rows ? r0 / p.group : -1, s1 = r1 < rows ? r1 / p.group : -1;
+  uint32_t qa[D / 16][4];
+  load_q<D>(qa, p.q, p.hq, s0, h * p.group + (r0 % p.group), s1, h * p.group + (r1 % p.group), p.qscale, lane);
+  float o[D / 8][4];
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-      for (int i = 0; i < nb; ++i) {
-        const int s = i % kStages;
-        if (!mbar_wait(&full[s], (i / kStages) & 1, 412)) {
-          // timed out (MG_ERR_TIMEOUT recorded): leave an empty state so the merge gives this slot no weight
-          m[0] = m[1] = -INFINITY;
-          l[0] = l[1] = 0.f;
-          break;
-        }
-        const uint32_t ks = smem_u32(smem + s * C::kStageBytes);
-        attend_tile<D>(qa, ks, ks + C::kTileBytes, 16, o, m, l, lane);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-      }
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  for (int i = 0; i < nb; ++i) {
+    if (!mbar_wait(&full[i], 0, 412)) {
+      // timed out (MG_ERR_TIMEOUT recorded): leave an empty state so the merge gives this slot no weight
+      m[0] = m[1] = -INFINITY;
+      l[0] = l[1] = 0.f;
+      break;
+    }
+    const uint32_t ks = smem_u32(smem + i * C::kStageBytes);
+    attend_tile<D>(qa, ks, ks + C::kTileBytes, 16, o, m, l, lane);
+  }
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int row = r ? r1 : r0;
-        if (row >= rows) continue;
-        const int seq = row / p.group, head = h * p.group + row % p.group;
-        const int64_t slot = ((int64_t)seq * p.hq + head) * p.nslots + chunk;
-        float* dst = p.ws_o + slot * D;
+  for (int r = 0; r < 2; ++r) {
+    const int row = r ? r1 : r0;
+    if (row >= rows) continue;
+    const int seq = row / p.group, head = h * p.group + row % p.group;
+    const int64_t slot = ((int64_t)seq * p.hq + head) * p.nslots + chunk;
+    float* dst = p.ws_o + slot * D;
 #pragma unroll
-        for (int dn = 0; dn < D / 8; ++dn) {
-          dst[dn * 8 + c] = o[dn][2 * r];
-          dst[dn * 8 + c + 1] = o[dn][2 * r + 1];
-        }
-        if ((lane & 3) == 0) {
-          p.ws_ml[slot * 2] = m[r];
-          p.ws_ml[slot * 2 + 1] = l[r];
-        }
-      }
+    for (int dn = 0; dn < D / 8; ++dn) {
+      dst[dn * 8 + c] = o[dn][2 * r];
+      dst[dn * 8 + c + 1] = o[dn][2 * r + 1];
+    }
+    if ((lane & 3) == 0) {
+      p.ws_ml[slot * 2] = m[r];
+      p.ws_ml[slot * 2 + 1] = l[r];
     }
   }
-  // count this CTA in for every sequence whose query rows it holds (it may finish several)
-  const int row_lo = rg * kRowsPerGroup, row_hi = min(rows, row_lo + kRowsPerGroup);
-  for (int seq = row_lo / p.group; seq * p.group < row_hi; ++seq)
-    arrive_and_merge<D>(p, seq, h, s_last, reinterpret_cast<float*>(smem));
 }
 
 template <int D, bool T>
@@ -595,24 +486,11 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(const __grid_co
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnCfg<D>::kBarOffset);
   uint64_t* empty = full + kStages;
-  __shared__ int s_last;
   griddep_launch();
-  const int n_shared_ctas = p.n_chunks * p.n_row_groups * p.hkv;
-  const bool is_shared = (int)blockIdx.x < n_shared_ctas;
-  const int per_head = p.n_chunks * p.n_row_groups;
-  const int sh_h = is_shared ? (int)blockIdx.x / per_head : 0;
-  const int sh_r = is_shared ? (int)blockIdx.x % per_head : 0;
   if (threadIdx.x == 0) {
-    // a private stage is released by the one warp that consumed it; a shared stage by every active consumer
-    uint32_t consumers = 1;
-    if (is_shared) {
-      const int rg = sh_r % p.n_row_groups;
-      const int rows_here = min(p.b * p.group - rg * kRowsPerGroup, kRowsPerGroup);
-      consumers = (uint32_t)((rows_here + 15) / 16);
-    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], consumers);
+      mbar_init(&empty[s], 1);
     }
     fence_mbar_init();
   }
@@ -622,26 +500,41 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(const __grid_co
   }
   __syncthreads();
   griddep_wait();
-  if (is_shared) {
-    shared_cta<D>(p, &tk, &tv, sh_h, sh_r / p.n_row_groups, sh_r % p.n_row_groups, smem, full, empty, &s_last);
+  const int n_shared_ctas = p.n_shared_ctas_per_head * p.n_row_groups * p.hkv;
+  if ((int)blockIdx.x < n_shared_ctas) {
+    const int per_head = p.n_shared_ctas_per_head * p.n_row_groups;
+    const int h = blockIdx.x / per_head, r = blockIdx.x % per_head;
+    shared_cta<D>(p, &tk, &tv, h, r / p.n_row_groups, r % p.n_row_groups, smem, full);
   } else {
     const int i = blockIdx.x - n_shared_ctas;
-    private_cta<D, T>(p, &tk, &tv, i / p.nsplit, i % p.nsplit, smem, full, empty, &s_last);
+    private_cta<D, T>(p, &tk, &tv, i / p.nsplit, i % p.nsplit, smem, full, empty);
   }
 }
 
+template <int D>
+__global__ void combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml, int nslots,
+                               __nv_bfloat16* __restrict__ out) {
+  griddep_launch();
+  griddep_wait();
+  const int64_t sh = blockIdx.x;  // seq * hq + head
+  const int d = threadIdx.x;
+  const float* ml = ws_ml + sh * nslots * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < nslots; ++s) M = fmaxf(M, ml[2 * s]);
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < nslots; ++s) {
+    const float w = M == -INFINITY ? 0.f : exp2f(ml[2 * s] - M);
+    L += ml[2 * s + 1] * w;
+    O += ws_o[(sh * nslots + s) * D + d] * w;
+  }
+  out[sh * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+}
+
 struct Plan {
-  int chunk, n_chunks, n_row_groups, nsplit, bps, nslots;
+  int n_shared_ctas_per_head, n_row_groups, nsplit, bps, nslots;
   bool direct;
   size_t ws_bytes;
 };
-
-// The merge tickets sit in a fixed region at the start of every workspace (one u32 per (sequence, kv
-// head), up to kMaxTickets pairs), the split slots after it. The region does not move with the launch's
-// sizes, so one workspace can serve launches of different shapes: a launch never writes slot data over
-// another shape's tickets.
-constexpr size_t kTicketBytes = 64 * 1024;
-constexpr int64_t kMaxTickets = kTicketBytes / sizeof(uint32_t);
 
 int sm_count_attn() {
   static int n = 0;
@@ -654,31 +547,25 @@ int sm_count_attn() {
   return n;
 }
 
-// One block count for every CTA: about two waves of three CTAs per SM over all block loads of the launch
-// (shared chunks are loaded once per row group), between 2 x kCons and 64 blocks per CTA. Shared chunks
-// and private splits then take about the same time, so no CTA kind leaves a long tail.
+// Splits: private CTAs for about two and a half waves of three CTAs per SM beside the shared CTAs
+// (small enough that the last wave's tail is short), with at least two tiles per consumer warp.
 Plan make_plan(int b, int hq, int hkv, int d, int max_blocks, int n_shared) {
   Plan pl{};
+  pl.n_shared_ctas_per_head = (n_shared + kChunk - 1) / kChunk;
   const int row_tiles = (b * (hq / hkv) + 15) / 16;
   pl.n_row_groups = (row_tiles + kCons - 1) / kCons;
   const int priv_max = max_blocks - n_shared > 0 ? max_blocks - n_shared : 1;
-  const int64_t loads = (int64_t)n_shared * hkv * pl.n_row_groups + (int64_t)b * hkv * priv_max;
-  const int64_t slots = 3LL * sm_count_attn();
-  int64_t per = (loads + 2 * slots - 1) / (2 * slots);
-  per = per < 2 * kCons ? 2 * kCons : (per > 64 ? 64 : per);
-  // the merge stages 2 x group x nslots floats in the ring's shared memory
-  const int64_t max_slots = (int64_t)kStages * 2 * 16 * d * 2 / (2 * 16 * 4);
-  while (per < 4096 && (n_shared + per - 1) / per + (priv_max + per - 1) / per > max_slots) per *= 2;
-  pl.chunk = n_shared > 0 ? (int)std::min<int64_t>(per, n_shared) : 1;
-  pl.n_chunks = n_shared > 0 ? (n_shared + pl.chunk - 1) / pl.chunk : 0;
-  if (pl.n_chunks) pl.chunk = (n_shared + pl.n_chunks - 1) / pl.n_chunks;  // even chunks
-  pl.nsplit = (int)((priv_max + per - 1) / per);
-  pl.bps = (priv_max + pl.nsplit - 1) / pl.nsplit;
+  const int pairs = b * hkv;
+  const int target = 15 * sm_count_attn() / 2 - pl.n_shared_ctas_per_head * pl.n_row_groups * hkv;
+  int nsplit = target > pairs ? (target + pairs - 1) / pairs : 1;
+  const int max_split = (priv_max + 2 * kCons - 1) / (2 * kCons);
+  nsplit = nsplit > max_split ? max_split : nsplit;
+  nsplit = nsplit < 1 ? 1 : nsplit;
+  pl.bps = (priv_max + nsplit - 1) / nsplit;
   pl.nsplit = (priv_max + pl.bps - 1) / pl.bps;
-  pl.nslots = pl.n_chunks + pl.nsplit;
+  pl.nslots = pl.n_shared_ctas_per_head + pl.nsplit;
   pl.direct = pl.nslots == 1;
-  const size_t slot_floats = (size_t)b * hq * pl.nslots * (size_t)(d + 2);
-  pl.ws_bytes = pl.direct ? 0 : kTicketBytes + slot_floats * sizeof(float);
+  pl.ws_bytes = pl.direct ? 0 : (size_t)b * hq * pl.nslots * (size_t)(d + 2) * sizeof(float);
   return pl;
 }
 
@@ -703,7 +590,10 @@ int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v
   if (rc) return rc;
   rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, v_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
   if (rc) return rc;
-  const int64_t ctas = (int64_t)pl.n_chunks * pl.n_row_groups * p.hkv + (int64_t)p.b * p.hkv * pl.nsplit;
+  p.n_shared_ctas_per_head = pl.n_shared_ctas_per_head;
+  p.n_row_groups = pl.n_row_groups;
+  const int64_t ctas = (int64_t)pl.n_shared_ctas_per_head * pl.n_row_groups * p.hkv +
+                       (int64_t)p.b * p.hkv * pl.nsplit;
   if (ctas > 0x7fffffff) return MG_ERR_UNSUPPORTED;
   if (p.group <= 8) {
     MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, true>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk, tv,
@@ -711,6 +601,10 @@ int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v
   } else {
     MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, false>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk,
                           tv, p));
+  }
+  if (!pl.direct) {
+    MG_CUDA_TRY(mg_launch(combine_kernel<D>, dim3((unsigned)(p.b * p.hq)), dim3(D), 0, st, 1, p.ws_o, p.ws_ml,
+                          pl.nslots, p.out));
   }
   return MG_OK;
 }
@@ -737,10 +631,8 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
     return MG_ERR_INVALID_ARG;
   if (d != 32 && d != 64 && d != 128) return MG_ERR_UNSUPPORTED;
   if (b == 0) return MG_OK;
-  if ((int64_t)b * hkv > kMaxTickets) return MG_ERR_UNSUPPORTED;
   const Plan pl = make_plan(b, hq, hkv, d, max_blocks, n_shared_blocks);
-  if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 15)))
-    return MG_ERR_INVALID_ARG;
+  if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes)) return MG_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) | reinterpret_cast<uintptr_t>(q)) & 15)
     return MG_ERR_INVALID_ARG;
   AttnParams p{};
@@ -754,17 +646,14 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
   p.hkv = hkv;
   p.group = hq / hkv;
   p.n_shared = n_shared_blocks;
-  p.chunk = pl.chunk;
-  p.n_chunks = pl.n_chunks;
-  p.n_row_groups = pl.n_row_groups;
+  p.n_shared_ctas_per_head = pl.n_shared_ctas_per_head;
   p.nsplit = pl.nsplit;
   p.bps = pl.bps;
   p.nslots = pl.nslots;
   p.qscale = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
-  p.tickets = pl.ws_bytes ? static_cast<uint32_t*>(workspace) : nullptr;
-  p.ws_o = pl.ws_bytes ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes) : nullptr;
-  p.ws_ml = pl.ws_bytes ? p.ws_o + (size_t)b * hq * pl.nslots * d : nullptr;
+  p.ws_o = static_cast<float*>(workspace);
+  p.ws_ml = pl.ws_bytes ? static_cast<float*>(workspace) + (size_t)b * hq * pl.nslots * d : nullptr;
   p.direct = pl.direct;
   cudaStream_t st = mg_stream(stream);
   if (d == 32) return launch_attn<32>(p, pl, k_pool, v_pool, st);
@@ -815,9 +704,8 @@ extern "C" int mg_paged_decode_attn_noalloc(const float* q, const void* k_pool, 
   void* scratch = nullptr;
   rc = noalloc_scratch_address(&scratch);
   if (rc) return rc;
-  // Every split slot the merge reads is written by this call's CTAs first. The per-(sequence, kv head)
-  // tickets start at zero (a device array is zero when the library loads) and every call leaves them at
-  // zero, so nothing needs clearing between calls.
+  // Every split slot the combine step reads is written by this call's attention CTAs first, so the
+  // previous call's contents never need clearing.
   return mg_paged_decode_attn(q, k_pool, v_pool, num_blocks, block_tables, max_blocks, ctx_lens, b, hq, hkv, d,
                               n_shared_blocks, scale, out, scratch, (size_t)MG_ATTN_NOALLOC_SCRATCH_BYTES, stream);
 }

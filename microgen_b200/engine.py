@@ -281,6 +281,83 @@ class DecodeEngine:
         if world > 1 and self.fused_allreduce_choice(group) and isinstance(weights.lm_q, K.PackedWeight) \
                 and spec.hidden % 128 == 0 and spec.hidden <= 8192:
             self.comm = K.Comm(rank, world, max_batch * spec.hidden, group=group)
+        # MG_BLOCK=1: the persistent layer kernel (one launch per layer boundary: o_proj, norm, MLP, norm,
+        # QKV + RoPE + KV append) where its shapes allow. Off by default: on the Llama-3.2-3B workload it
+        # measured slower than the kernel-per-op step (bound by its tensor-core issue rate at 32 tokens and by
+        # the activation reads at each phase start).
+        self.block_args = None
+        if self.block_supported(world):
+            self._init_block()
+
+    def block_supported(self, world: int) -> bool:
+        s, w = self.spec, self.w
+        if os.environ.get("MG_BLOCK", "0") != "1" or not isinstance(w.lm_q, K.PackedWeight):
+            return False
+        if self.max_batch > K.BLOCK_MAX_TOKENS or s.hidden % 128 or self.D not in (32, 64, 128):
+            return False
+        if world > 1 and self.comm is None:
+            return False
+        L = w.layers[0]
+        return L.gu_q.shape[0] % 128 == 0 and L.o_q.shape[1] % 16 == 0 and L.d_q.shape[1] % 16 == 0
+
+    def _init_block(self) -> None:
+        """One mg_block_args per layer boundary: [0] = input norm + QKV of layer 0; [l+1] = o_proj, MLP and
+        the next input norm (the final norm after the last layer) + the next layer's QKV."""
+        s, w, dev = self.spec, self.w, self.device
+        B, H = self.max_batch, s.hidden
+        self.x2 = torch.zeros((B, H), dtype=torch.bfloat16, device=dev)
+        norm = K.NORM_LAYER if s.family == "gpt2" else K.NORM_RMS
+        mlp = K.EPI_GELU_BF16 if s.family == "gpt2" else K.EPI_SWIGLU_BF16
+        ptr = lambda t: 0 if t is None else t.data_ptr()
+        nL = len(w.layers)
+        args = []
+        for i in range(nL + 1):
+            a = K.BlockArgs()
+            a.m, a.hidden, a.hq, a.hkv, a.head_dim = B, H, self.hq, self.hkv, self.D
+            a.norm, a.mlp, a.eps = norm, mlp, float(s.eps)
+            a.h, a.attn, a.x2, a.act, a.x1 = ptr(self.h), ptr(self.attn), ptr(self.x2), ptr(self.act), ptr(self.x)
+            a.positions, a.slots, a.q_out = ptr(self.positions), ptr(self.slots), ptr(self.q)
+            if self.cos_sin is not None:
+                a.cos_sin, a.max_pos = ptr(self.cos_sin), self.cos_sin.shape[0]
+            flags = 0
+            if i > 0:  # o_proj + MLP of layer i-1
+                P = w.layers[i - 1]
+                flags |= K.BLK_O | K.BLK_MLP
+                a.o = K.block_linear(P.o_q, P.o_s, P.o_b)
+                a.gate_up = K.block_linear(P.gu_q, P.gu_s, P.gu_b)
+                a.down = K.block_linear(P.d_q, P.d_s, P.d_b)
+                a.n2_w, a.n2_b = ptr(P.ln2_w), ptr(P.ln2_b)
+            flags |= K.BLK_N1
+            if i < nL:  # input norm + QKV of layer i
+                N = w.layers[i]
+                flags |= K.BLK_QKV
+                a.n1_w, a.n1_b = ptr(N.ln1_w), ptr(N.ln1_b)
+                a.qkv = K.block_linear(N.qkv_q, N.qkv_s, N.qkv_b)
+                a.k_pool, a.v_pool = ptr(self.pool.k[i]), ptr(self.pool.v[i])
+                a.num_blocks = self.pool.k[i].shape[0]
+            else:      # final norm (lm_head input)
+                a.n1_w, a.n1_b = ptr(w.norm_w), ptr(w.norm_b)
+            a.flags = flags
+            args.append(a)
+        need = max(K.block_workspace_bytes(a) for a in args)
+        self.block_ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        self.block_args = args
+
+    def block_bytes(self, i: int, b: int) -> int:
+        """Algorithmic bytes of block launch ``i`` at batch ``b``: INT8 codes + scales of its linears, the
+        activations each linear reads (bf16) and writes, the residual read and written per norm."""
+        w, H = self.w, self.spec.hidden
+        n = 0
+        if i > 0:
+            P = w.layers[i - 1]
+            n += self.linear_bytes(P.o_q, b, 8, H) + self.linear_bytes(P.gu_q, b, 2, self.act.shape[1])
+            n += self.linear_bytes(P.d_q, b, 8, H) + b * H * 6
+        n += b * H * 6
+        if i < len(w.layers):
+            N = w.layers[i]
+            nq = (self.hq + 2 * self.hkv) * self.D
+            n += self.linear_bytes(N.qkv_q, b, 0, nq) + b * self.hq * self.D * 4 + b * 2 * self.hkv * self.D * 2
+        return n
 
     @staticmethod
     def fused_allreduce_choice(group=None) -> bool:
@@ -323,6 +400,24 @@ class DecodeEngine:
         attn_bytes = kv_tokens * self.hkv * D * 2 * 2 + b * self.hq * D * (4 + 2)
         with P("embed", b * H * 8):
             K.embed(self.tokens[:b], self.positions[:b], w.embed, w.wpe, h)
+        if self.block_args is not None:
+            comm = self.comm
+            for i, a in enumerate(self.block_args):
+                if i > 0:
+                    l = i - 1
+                    with P("paged_attn", attn_bytes):
+                        K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
+                                            n_shared_blocks=n_shared_blocks, out=self.attn[:b],
+                                            workspace=self.workspace, validate=False)
+                a.m = b
+                with P("decode_block", self.block_bytes(i, b)):
+                    K.decode_block(a, self.block_ws, comm)
+            if compute_logits:
+                with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, s.vocab)):
+                    K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32)
+                with P("argmax", b * s.vocab * 4):
+                    K.argmax_rows(self.logits[:b], out=self.next_tokens[:b])
+            return
         fused = self.comm is not None
         norm_kind = K.NORM_LAYER if s.family == "gpt2" else K.NORM_RMS
         push_bytes = b * H * 4 * self.world

@@ -165,8 +165,7 @@ def attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks=0) -> int:
 def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared_blocks=0, out=None,
                       workspace=None, validate=True):
     """q fp32 [b, hq, d]; pools bf16 [nblk, hkv, 16, d]; tables int32 [b, max_blocks]; ctx int32 [b].
-    Returns bf16 [b, hq*d]. ``workspace`` (optional; allocated when missing) must be zero-filled before its
-    first use: the kernel's merge tickets live in it and every launch leaves them at zero.
+    Returns bf16 [b, hq*d]. ``workspace`` (optional) is allocated when missing or too small.
 
     With ``n_shared_blocks`` > 0 the first that many entries of every table must equal row 0's (the
     kernel reads the shared blocks once, from row 0); ``validate`` checks this before the launch and raises
@@ -192,6 +191,8 @@ def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared
     _lib.call("mg_paged_decode_attn", _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables),
               max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks, float(scale), _ptr(out),
               _ptr(workspace if ws else None), ws, _stream())
+    if ws:
+        _lib.LAUNCHES[0] += 1  # the split-combine kernel
     return out
 
 
@@ -312,3 +313,63 @@ def rowpar_reduce_norm(comm: Comm, h, bias, norm: int, w=None, b=None, eps: floa
     _lib.call("mg_rowpar_reduce_norm", comm.handle, _ptr(h), _ptr(bias), m, n, int(norm), _ptr(w), _ptr(b),
               float(eps), _ptr(x), _stream())
     return x
+
+
+# ---- persistent decode layer (mg_decode_block) -----------------------------------------------------
+BLK_O, BLK_MLP, BLK_N1, BLK_QKV = 1, 2, 4, 8
+BLOCK_MAX_TOKENS = 32
+
+
+class BlockLinear(C.Structure):
+    _fields_ = [("packed", C.c_void_p), ("scales", C.c_void_p), ("bias", C.c_void_p), ("n", C.c_int64),
+                ("k", C.c_int64)]
+
+
+class BlockArgs(C.Structure):
+    """ctypes mirror of ``mg_block_args`` (include/microgen_b200.h)."""
+    _fields_ = [("m", C.c_int), ("flags", C.c_int), ("hidden", C.c_int), ("hq", C.c_int), ("hkv", C.c_int),
+                ("head_dim", C.c_int), ("norm", C.c_int), ("mlp", C.c_int), ("eps", C.c_float),
+                ("max_pos", C.c_int), ("o", BlockLinear), ("gate_up", BlockLinear), ("down", BlockLinear),
+                ("qkv", BlockLinear), ("h", C.c_void_p), ("attn", C.c_void_p), ("n2_w", C.c_void_p),
+                ("n2_b", C.c_void_p), ("x2", C.c_void_p), ("act", C.c_void_p), ("n1_w", C.c_void_p),
+                ("n1_b", C.c_void_p), ("x1", C.c_void_p), ("cos_sin", C.c_void_p), ("positions", C.c_void_p),
+                ("slots", C.c_void_p), ("q_out", C.c_void_p), ("k_pool", C.c_void_p), ("v_pool", C.c_void_p),
+                ("num_blocks", C.c_int64)]
+
+
+def block_linear(q: PackedWeight, scales: torch.Tensor, bias: torch.Tensor | None) -> BlockLinear:
+    if not isinstance(q, PackedWeight):
+        raise TypeError("the persistent layer kernel reads tile-packed codes (pack_weights)")
+    _need(scales, torch.float32, "scales")
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+    return BlockLinear(q.data.data_ptr(), scales.data_ptr(), 0 if bias is None else bias.data_ptr(), q.n, q.k)
+
+
+def block_workspace_bytes(args: BlockArgs) -> int:
+    n = C.c_size_t(0)
+    _lib.call("mg_decode_block_workspace_bytes", C.byref(args), C.byref(n))
+    return int(n.value)
+
+
+def decode_block(args: BlockArgs, workspace: torch.Tensor, comm=None) -> None:
+    """One launch of the persistent decode layer described by ``args`` (see ``mg_decode_block``).
+    ``workspace``: a zero-filled uint8 device tensor of at least ``block_workspace_bytes(args)`` bytes,
+    reused across launches; ``comm``: the row-parallel communicator at world > 1."""
+    _lib.call("mg_decode_block", C.byref(args), C.c_void_p(comm.handle if comm is not None else 0),
+              _ptr(workspace), workspace.numel(), _stream())
+
+
+def decode_block_diag(clear: bool = True) -> list[int]:
+    """The snapshot of the first persistent-layer wait that gave up (see ``mg_decode_block_diag``)."""
+    buf = (C.c_uint32 * (32 + 1024))()
+    _lib.call("mg_decode_block_diag", C.cast(buf, C.c_void_p), 1 if clear else 0)
+    return list(buf)
+
+
+def decode_block_trace(ctas: int):
+    """numpy int64 [ctas, 16]: globaltimer stamps of the latest persistent-layer launch (mg_decode_block_trace)."""
+    import numpy as np
+    out = np.zeros((ctas, 16), dtype=np.uint64)
+    _lib.call("mg_decode_block_trace", C.c_void_p(out.ctypes.data), int(ctas))
+    return out.astype(np.int64)

@@ -15,8 +15,13 @@ What is asserted, per sequence:
 * teacher-forced (the reference's tokens fed back): the argmax equals the reference's token at every
   step whose margin is at least DELTA_TF, and the sampled logits of the first four steps are within the
   model-level tolerance |err| <= MODEL_ATOL + 2e-2 |ref|. The contract's 1e-2 absolute bound is per
-  kernel (one linear, one attention); logits come out of 24-28 layers of bf16 activations, whose
-  rounding compounds: MODEL_ATOL is four times the per-kernel bound (measured: up to 0.019).
+  kernel (one linear, one attention); logits come out of 12-28 layers of bf16 activations, whose
+  rounding compounds. How much is measured, not guessed: ``tests/golden/bf16_sensitivity.py`` replays each
+  fixture's prefill on the CPU with exactly the B200 path's bf16 rounding points and writes the largest
+  deviation from the reference's fp32 logits to ``full_<shape>_bf16.json`` (GPT-2-small 0.009,
+  Qwen2.5-0.5B 0.020, Llama-3.2-3B 0.107; the fp32 replay itself is within 2e-5). MODEL_ATOL is twice
+  that deviation (the GPU adds rounding points of its own: bf16 q and probabilities inside the attention
+  MMAs), and at least four times the per-kernel bound; DELTA_TF is that deviation, at least 0.05.
 The steps exempted as near-ties and the largest logit errors are printed (pytest -s) so a run records them."""
 
 import json
@@ -28,9 +33,13 @@ import torch
 
 pytestmark = pytest.mark.gpu
 G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-RTOL, MODEL_ATOL = 2e-2, 4e-2
-DELTA = 0.02      # free-running: margins below this are near-ties (2 x the contract's per-kernel bound)
-DELTA_TF = 0.05   # teacher-forced argmax check: margins below this may flip within MODEL_ATOL
+RTOL = 2e-2
+
+
+def bf16_deviation(name: str) -> float:
+    """Largest logit deviation that bf16 activations alone cause at this shape (bf16_sensitivity.py)."""
+    with open(os.path.join(G, f"full_{name}_bf16.json")) as f:
+        return float(json.load(f)["bf16_max_dev"])
 
 
 def _backend(name):
@@ -51,6 +60,12 @@ def test_full_shape_greedy_stream_vs_reference(name):
     if not os.path.exists(os.path.join(G, f"full_{name}.npz")):
         pytest.skip(f"fixture full_{name}.npz not generated")
     be, d = _backend(name)
+    dev = bf16_deviation(name)
+    MODEL_ATOL = max(4e-2, 2.0 * dev)
+    # free-running: margins below DELTA are near-ties (2 x the contract's per-kernel bound, or half the
+    # largest bf16 deviation: the typical deviation is about a fifth of the largest)
+    DELTA = max(0.02, 0.5 * dev)
+    DELTA_TF = max(0.05, dev)  # teacher-forced argmax check: smaller margins may flip within MODEL_ATOL
     ref_tok, margins = d["tokens"], d["margins"]
     prompts = torch.tensor(d["prompts"])
     B, N = ref_tok.shape
