@@ -78,8 +78,8 @@ def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps:
         lin.append((eng.x[:b], L.gu_q, L.gu_s, L.gu_b, eng.act[:b], epi_mlp,
                     eng.linear_bytes(L.gu_q, b, 2, eng.act.shape[1])))
         lin.append((eng.act[:b], L.d_q, L.d_s, None, scratch, K.EPI_ADD_F32, eng.linear_bytes(L.d_q, b, 8, H)))
-    lin.append((eng.x[:b], w.lm_q, w.lm_s, None, eng.logits[:b], K.EPI_STORE_F32,
-                eng.linear_bytes(w.lm_q, b, 4, spec.vocab)))
+    lin.append((eng.x[:b], w.lm_q, w.lm_s, None, eng.logits[:b, :eng.vocab_local], K.EPI_STORE_F32,
+                eng.linear_bytes(w.lm_q, b, 4, eng.vocab_local)))
     tab, ctx = eng.tables[:b], eng.ctx[:b]
     attn_bytes = kv_tokens * eng.hkv * eng.D * 2 * 2 + b * eng.hq * eng.D * (4 + 2)
 
@@ -661,11 +661,15 @@ def main():
         nvlink = push_chain(eng, spec, B)
     dom = max(chains, key=lambda k: chains[k]["us_per_step"])
     achieved = chains[dom]["gbs"]
+    # DRAM bytes per launch: the committed capture's DRAM / algorithmic ratio for this kernel family times this
+    # run's algorithmic bytes per launch (the capture ran at TP=1 on a 2-layer cut of the same shapes)
     traffic = None
     tr_path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
     if os.path.exists(tr_path):
         try:
-            traffic = json.load(open(tr_path)).get(f"{args.workload}:{dom}")
+            tr = json.load(open(tr_path)).get(f"{args.workload}:{dom}")
+            if tr:
+                traffic = int(round(tr["dram_bytes"] / tr["algorithmic_bytes"] * chains[dom]["bytes_per_launch"]))
         except Exception:
             traffic = None
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",

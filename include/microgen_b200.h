@@ -117,6 +117,17 @@ int mg_i8_linear_packed_rowpar(const void* x, int64_t m, int64_t k, int64_t ldx,
                                const float* scales, int64_t n, void* comm, int split_k, void* stream);
 int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, int m, int n, int norm, const float* w,
                           const float* wb, float eps, void* x, void* stream);
+/* Greedy argmax over a vocab-parallel lm_head (pytorch.py:153-155 torch.argmax over logits whose columns
+ * are split across the ranks in rank order, each rank holding lm_head rows [offset, offset + n_local) —
+ * the reference's split rule, n // world with the remainder on the last rank). logits: this rank's fp32
+ * [m, n_local] shard (row stride ld). Finds each row's first maximal local column, exchanges {value,
+ * global index} with every rank through the communicator's receive areas (two epoch-tagged words per row,
+ * the same epoch sequence as the row-parallel pushes, so every rank must make this call at the same point
+ * of that sequence), and writes idx[i] = the global first maximal index of row i, identical on every rank.
+ * m <= 1024 and 2 * m <= slot words. A peer that never publishes makes the wait give up after the
+ * communicator's limit (MG_ERR_TIMEOUT in the device error word). */
+int mg_vocab_argmax(void* comm, const float* logits, int m, int64_t n_local, int64_t ld, int64_t offset,
+                    int32_t* idx, void* stream);
 /* mg_i8_linear_packed_rowpar on the stream-K kernel (workspace as for mg_i8_linear_packed_sk). */
 int mg_i8_linear_packed_rowpar_sk(const void* x, int64_t m, int64_t k, int64_t ldx, const int8_t* packed,
                                   const float* scales, int64_t n, void* comm, void* workspace,

@@ -57,6 +57,7 @@ SIGNATURES = {
     "mg_rmsnorm": [_p, _p, _i, _i, _f, _p, _p],
     "mg_layernorm": [_p, _p, _p, _i, _i, _f, _p, _p],
     "mg_argmax_rows": [_p, _i, _i64, _i64, _p, _p],
+    "mg_vocab_argmax": [_p, _p, _i, _i64, _i64, _i64, _p, _p],
     "mg_decode_advance": [_p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mg_decode_block_workspace_bytes": [_p, C.POINTER(C.c_size_t)],
     "mg_decode_block": [_p, _p, _p, _sz, _p],
@@ -72,7 +73,7 @@ LAUNCHING = {"mg_quantize_rows_i8", "mg_i8_linear", "mg_i8_linear_simt", "mg_i8_
              "mg_i8_linear_packed_rowpar", "mg_rowpar_reduce_norm", "mg_i8_linear_packed_sk",
              "mg_i8_linear_packed_rowpar_sk",
              "mg_paged_decode_attn", "mg_embed", "mg_rmsnorm", "mg_layernorm", "mg_argmax_rows",
-             "mg_decode_advance", "mg_decode_block"}
+             "mg_decode_advance", "mg_decode_block", "mg_vocab_argmax"}
 LAUNCHES = [0]  # kernels launched (or captured) through call() in this process
 
 _lock = threading.Lock()

@@ -11,8 +11,10 @@ The cache object is a ``PagedKVCache``: the block tables of the batch's sequence
 the backend's ``PagedKVCacheAllocator`` (whose device pool holds K/V). The caller
 owns it and passes it back in, as with ``KVCacheState``.
 
-Prefill runs the prompt through the decode kernels one position at a time (all
-sequences of the batch per launch). Prompts that share a leading run of whole
+Prefill runs ``prefill_chunk`` positions of every prompt per pass: each INT8 linear
+on all those tokens in one launch (tcgen05 tiles of up to 256 tokens), causal
+attention per prompt on the paged decode kernel (``DecodeEngine.prefill``). Prompts
+that share a leading run of whole
 16-token blocks are prefilled once for that prefix (batch 1) and the blocks are
 shared by reference count; the attention kernel then reads them once per batch.
 With ``prefix_cache_capacity`` > 0 such prefixes are also kept across calls
@@ -100,7 +102,7 @@ class B200QuantizedBackend:
     def __init__(self, device=None, quant_type: str = "int8", max_batch: int = 64, max_seq_len: int = 4096,
                  num_blocks: Optional[int] = None, use_cuda_graph: bool = True, free_list_seed: Optional[int] = None,
                  world_size: int = 1, group=None, device_check_every: int = 1,
-                 prefix_cache_capacity: int = 0) -> None:
+                 prefix_cache_capacity: int = 0, prefill_chunk: int = 64) -> None:
         """``device_check_every``: after every that many ``decode`` calls, read the library's device error
         word (one stream synchronisation) and raise — TimeoutError when a bounded wait gave up (a peer
         rank that never pushed its row-parallel partial), RuntimeError for a failed device-side check —
@@ -108,7 +110,11 @@ class B200QuantizedBackend:
 
         ``prefix_cache_capacity`` > 0 keeps a block-level prefix cache (``PagedPrefixCache``) of that many
         entries: a prefill whose prompts start with a cached run of whole blocks shares those blocks instead
-        of recomputing them, and every prefill's whole-block common prefix is cached for later calls."""
+        of recomputing them, and every prefill's whole-block common prefix is cached for later calls.
+
+        ``prefill_chunk``: prompt positions per prefill pass (every prompt of the batch at once, the
+        linears on all those tokens per launch); 0 runs the prompt through the decode step one position at
+        a time."""
         if quant_type.lower() != "int8":
             raise ValueError("the B200 decode path implements INT8 per-channel weights only")
         if isinstance(device, CUDADeviceInfo):
@@ -124,7 +130,9 @@ class B200QuantizedBackend:
         self.world_size, self.group = world_size, group
         self.device_check_every = max(0, int(device_check_every))
         self._decodes = 0
+        self._greedy = None
         self.prefix_cache_capacity = int(prefix_cache_capacity)
+        self.prefill_chunk = max(0, int(prefill_chunk))
         self.prefix_cache: Optional[PagedPrefixCache] = None
         self.rank = torch.distributed.get_rank(group) if world_size > 1 else 0
         self.engine: Optional[DecodeEngine] = None
@@ -149,7 +157,9 @@ class B200QuantizedBackend:
         """Load from a ModelSpec and a state dict keyed by HF parameter names (any device, fp32)."""
         dev = self._device.torch_device
         with torch.cuda.device(dev):
-            weights = WeightLoader(spec, dev, self.rank, self.world_size).load(state)
+            # lm_head split by rows across the ranks (MG_VOCAB_PARALLEL=0 replicates it, as the reference does)
+            vp = self.world_size > 1 and DecodeEngine.rank0_flag("MG_VOCAB_PARALLEL", self.group)
+            weights = WeightLoader(spec, dev, self.rank, self.world_size, vocab_parallel=vp).load(state)
             max_blocks = (self.max_seq_len + BLOCK - 1) // BLOCK
             self.engine = DecodeEngine(spec, weights, dev, self.max_batch, self.num_blocks, max_blocks,
                                        rank=self.rank, world=self.world_size, group=self.group,
@@ -223,8 +233,12 @@ class B200QuantizedBackend:
                     else:
                         cache.prefix = self.allocator.allocate_sequence("prefix", n_prefix * BLOCK)
                     prefix_mirror = TableMirror(1, eng.max_blocks)
-                    for p in range(reused * BLOCK, n_prefix * BLOCK):
-                        self._run([cache.prefix], [ids[0][p]], [p], 0, logits=False, cache_mirror=prefix_mirror)
+                    if self.prefill_chunk and n_prefix > reused:
+                        eng.prefill([ids[0]], prefix_mirror.update([cache.prefix]), reused * BLOCK, n_prefix * BLOCK,
+                                    compute_logits=False, chunk=self.prefill_chunk)
+                    else:
+                        for p in range(reused * BLOCK, n_prefix * BLOCK):
+                            self._run([cache.prefix], [ids[0][p]], [p], 0, logits=False, cache_mirror=prefix_mirror)
                     if self.prefix_cache is not None:
                         self.prefix_cache.insert(toks, cache.prefix)
                     cache.tables = [self.allocator.share_prefix(cache.prefix, n_prefix, f"seq{i}", T)
@@ -246,10 +260,25 @@ class B200QuantizedBackend:
                 T = start + T
             if cache.mirror is None or cache.mirror.arr.shape[0] < b:
                 cache.mirror = TableMirror(b, eng.max_blocks)
-            for p in range(start, T):
-                self._run(cache.tables, [r[p] for r in ids], [p] * b, cache.n_shared_blocks, logits=(p == T - 1),
-                          cache_mirror=cache.mirror)
-            return eng.logits[:b].clone(), cache
+            if self.prefill_chunk:
+                width = max(t.num_blocks() for t in cache.tables)
+                if width > eng.max_blocks:
+                    raise ValueError(f"context of {width * BLOCK} tokens exceeds max_seq_len {self.max_seq_len}")
+                eng.prefill(ids, cache.mirror.update(cache.tables), start, T, compute_logits=True,
+                            chunk=self.prefill_chunk)
+            else:
+                for p in range(start, T):
+                    self._run(cache.tables, [r[p] for r in ids], [p] * b, cache.n_shared_blocks,
+                              logits=(p == T - 1), cache_mirror=cache.mirror)
+            return self._logits_out(b), cache
+
+    def _logits_out(self, b: int) -> torch.Tensor:
+        """The step's full logits for the caller, remembering the greedy tokens the step already computed
+        on the device so that ``sample`` of these unmodified logits needs no second argmax."""
+        eng = self.engine
+        out = eng.full_logits(b)
+        self._greedy = (out, out._version, eng.next_tokens[:b].clone())
+        return out
 
     def decode(self, token_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                cache: Optional[PagedKVCache] = None) -> Tuple[torch.Tensor, PagedKVCache]:
@@ -271,12 +300,15 @@ class B200QuantizedBackend:
             self._decodes += 1
             if self.device_check_every and self._decodes % self.device_check_every == 0:
                 K.check_device()
-            return eng.logits[:b].clone(), cache
+            return self._logits_out(b), cache
 
     def sample(self, logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0,
                top_p: float = 0.0) -> torch.Tensor:
         """Greedy on the device argmax kernel; otherwise the reference's sampling (``pytorch.py:145-177``)."""
         if temperature <= 0.0 or (top_k == 0 and top_p == 0.0 and temperature == 1.0):
+            g = self._greedy
+            if g is not None and logits is g[0] and logits._version == g[1]:
+                return g[2].to(torch.int64)[:, None]  # the device argmax of exactly these logits
             lg = logits.to(torch.float32).contiguous()
             return K.argmax_rows(lg).to(torch.int64)[:, None]
         logits = logits / max(temperature, 1e-5)

@@ -20,8 +20,8 @@
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMaxV = 8;                     // float4 per thread: rows up to 8192
+constexpr int kThreads = 1024;              // most: one float4 of a row per thread at hidden <= 4096
+constexpr int kMaxV = 2;                     // float4 per thread: rows up to 8192
 // A peer that has not pushed within the communicator's limit is reported: MG_PEER_TIMEOUT_MS in the
 // environment of mg_comm_create (default 1000 ms; ranks whose host sides drift apart by more than that,
 // e.g. through uneven start-up work, need a larger value).
@@ -75,7 +75,9 @@ __device__ __forceinline__ void wait_words(const uint64_t* p, uint32_t epoch, ui
   }
 }
 
-// One CTA per token row. norm: 0 = none, 1 = RMSNorm (w), 2 = LayerNorm (w, wb).
+// One CTA per token row (blockDim: the row's float4 count rounded up to a warp, at most kThreads).
+// Each thread loads its words from every rank before it consumes any, so the world's words cost one
+// memory round trip rather than one per rank. norm: 0 = none, 1 = RMSNorm (w), 2 = LayerNorm (w, wb).
 __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po, float* __restrict__ h,
                                                                        const float* __restrict__ bias, int n,
                                                                        int norm, const float* __restrict__ w,
@@ -95,16 +97,22 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
   float s1 = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxV; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
+    const int idx = threadIdx.x + i * blockDim.x;
     if (idx < nv) {
       float4 a = reinterpret_cast<const float4*>(hr)[idx];
-      for (int r = 0; r < po.world; ++r) {
-        uint64_t wd[2];
-        wait_words(recv + (int64_t)r * po.slot + idx * 2, epoch, wd, t0, dead, r, po.timeout_ns);
-        a.x += bf16lo((uint32_t)wd[0]);
-        a.y += bf16hi((uint32_t)wd[0]);
-        a.z += bf16lo((uint32_t)wd[1]);
-        a.w += bf16hi((uint32_t)wd[1]);
+      uint64_t wd[MG_MAX_RANKS][2];
+#pragma unroll
+      for (int r = 0; r < MG_MAX_RANKS; ++r)  // every rank's words in flight at once
+        if (r < po.world) ld_volatile_v2u64(recv + (int64_t)r * po.slot + idx * 2, wd[r][0], wd[r][1]);
+#pragma unroll
+      for (int r = 0; r < MG_MAX_RANKS; ++r) {
+        if (r >= po.world) break;
+        if ((uint32_t)(wd[r][0] >> 32) != epoch || (uint32_t)(wd[r][1] >> 32) != epoch)
+          wait_words(recv + (int64_t)r * po.slot + idx * 2, epoch, wd[r], t0, dead, r, po.timeout_ns);
+        a.x += bf16lo((uint32_t)wd[r][0]);
+        a.y += bf16hi((uint32_t)wd[r][0]);
+        a.z += bf16lo((uint32_t)wd[r][1]);
+        a.w += bf16hi((uint32_t)wd[r][1]);
       }
       if (bias) {
         const float4 b = reinterpret_cast<const float4*>(bias)[idx];
@@ -127,7 +135,7 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
     float s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxV; ++i) {
-      const int idx = threadIdx.x + i * kThreads;
+      const int idx = threadIdx.x + i * blockDim.x;
       if (idx < nv) {
         const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
         s2 += a * a + b * b + c * c + d * d;
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
   __nv_bfloat16* xr = x + row * n;
 #pragma unroll
   for (int i = 0; i < kMaxV; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
+    const int idx = threadIdx.x + i * blockDim.x;
     if (idx < nv) {
       const float4 g = reinterpret_cast<const float4*>(w)[idx];
       float4 o;
@@ -155,6 +163,61 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
       reinterpret_cast<uint2*>(xr)[idx] = u;
     }
   }
+}
+
+// Greedy argmax over a vocab-parallel lm_head: rank r holds logits columns [offset_r, offset_r + n_r) of
+// every row, in rank order. idx[i] enters as this rank's first maximal column of row i (mg_argmax_rows over
+// the shard). Each row's {value, global index} goes to slot [e%2][my rank] of every rank's receive area as two
+// words tagged with epoch e (e = this rank's count + 1, the same sequence the row-parallel pushes use); then
+// each row waits for the world's records (bounded by time), keeps the largest value, the smallest global
+// index on ties (torch.argmax's first maximal index over the whole row, pytorch.py:153-155), and the count
+// advances to e. One CTA, one thread per row.
+__global__ void __launch_bounds__(1024) vocab_argmax_merge_kernel(PeerOut po, const float* __restrict__ logits,
+                                                                   int64_t ld, int64_t n_local, int64_t offset,
+                                                                   int32_t* __restrict__ idx, int m) {
+  griddep_launch();
+  griddep_wait();
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(po.count) + 1u;
+  const uint64_t tag = (uint64_t)epoch << 32;
+  const int i = threadIdx.x;
+  if (i < m) {
+    int32_t li = idx[i];
+    float v = -INFINITY;
+    if (li >= 0 && li < n_local) {
+      v = logits[(int64_t)i * ld + li];
+    } else {
+      mg_record_error(MG_ERR_DEVICE, 660);
+      li = 0;
+    }
+    const int64_t off = ((int64_t)(epoch & 1u) * po.world + po.rank) * po.slot + 2 * (int64_t)i;
+    const uint64_t w0 = tag | __float_as_uint(v), w1 = tag | (uint32_t)(li + offset);
+    for (int r = 0; r < po.world; ++r) st_volatile_v2u64(po.recv[r] + off, w0, w1);
+    const uint64_t* recv = po.recv[po.rank] + (int64_t)(epoch & 1u) * po.world * po.slot + 2 * (int64_t)i;
+    float best = -INFINITY;
+    int32_t bi = 0x7fffffff;
+    uint64_t t0 = 0;
+    bool dead = false;
+    uint64_t wd[MG_MAX_RANKS][2];
+#pragma unroll
+    for (int r = 0; r < MG_MAX_RANKS; ++r)  // every rank's record in flight at once
+      if (r < po.world) ld_volatile_v2u64(recv + (int64_t)r * po.slot, wd[r][0], wd[r][1]);
+#pragma unroll
+    for (int r = 0; r < MG_MAX_RANKS; ++r) {
+      if (r >= po.world) break;
+      if ((uint32_t)(wd[r][0] >> 32) != epoch || (uint32_t)(wd[r][1] >> 32) != epoch)
+        wait_words(recv + (int64_t)r * po.slot, epoch, wd[r], t0, dead, r, po.timeout_ns);
+      if (dead) break;
+      const float rv = __uint_as_float((uint32_t)wd[r][0]);
+      const int32_t ri = (int32_t)(uint32_t)wd[r][1];
+      if (rv > best || (rv == best && ri < bi)) {
+        best = rv;
+        bi = ri;
+      }
+    }
+    idx[i] = bi == 0x7fffffff ? 0 : bi;
+  }
+  __syncthreads();  // every thread has read the count
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(po.count) = epoch;
 }
 
 }  // namespace
@@ -249,7 +312,25 @@ extern "C" int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, in
        reinterpret_cast<uintptr_t>(wb) | reinterpret_cast<uintptr_t>(x)) & 15)
     return MG_ERR_INVALID_ARG;
   if (m == 0) return MG_OK;
-  MG_CUDA_TRY(mg_launch(rowpar_reduce_norm_kernel, dim3(m), dim3(kThreads), 0, mg_stream(stream), 1, po, h, bias,
+  const int nv = n / 4;
+  const int threads = nv >= kThreads ? kThreads : (nv + 31) / 32 * 32;
+  MG_CUDA_TRY(mg_launch(rowpar_reduce_norm_kernel, dim3(m), dim3(threads), 0, mg_stream(stream), 1, po, h, bias,
                         n, norm, w, wb, eps, static_cast<__nv_bfloat16*>(x)));
+  return MG_OK;
+}
+
+extern "C" int mg_vocab_argmax(void* comm, const float* logits, int m, int64_t n_local, int64_t ld, int64_t offset,
+                               int32_t* idx, void* stream) {
+  PeerOut po;
+  int rc = mg_comm_peer_out(comm, &po);
+  if (rc) return rc;
+  if (!logits || !idx || m < 0 || m > 1024 || n_local <= 0 || ld < n_local || offset < 0 ||
+      offset + n_local > 0x7fffffff || 2 * (int64_t)m > po.slot)
+    return MG_ERR_INVALID_ARG;
+  if (m == 0) return MG_OK;
+  rc = mg_argmax_rows(logits, m, n_local, ld, idx, stream);
+  if (rc) return rc;
+  MG_CUDA_TRY(mg_launch(vocab_argmax_merge_kernel, dim3(1), dim3((unsigned)((m + 31) / 32 * 32)), 0,
+                        mg_stream(stream), 1, po, logits, ld, n_local, offset, idx, m));
   return MG_OK;
 }

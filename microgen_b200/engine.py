@@ -65,6 +65,9 @@ class ModelWeights:
     lm_q: torch.Tensor
     lm_s: torch.Tensor
     layers: list = field(default_factory=list)
+    # vocab-parallel lm_head: this rank holds rows [lm_offset, lm_offset + lm_s.numel()) of the full head
+    vocab_parallel: bool = False
+    lm_offset: int = 0
 
     def nbytes(self) -> int:
         n = 0
@@ -111,14 +114,41 @@ def row_parallel_residual(h: torch.Tensor, launch, rank: int, world: int, group=
         torch.distributed.all_reduce(h, group=group)
 
 
+def vocab_bounds(vocab: int, world: int) -> list[tuple[int, int]]:
+    """[start, end) of each rank's lm_head rows: the reference's split rule for sharded linears
+    (``N // world`` rows per rank, the last rank taking the remainder; ``parallel.py:19-24``)."""
+    per = vocab // world
+    return [(r * per, (r + 1) * per if r < world - 1 else vocab) for r in range(world)]
+
+
+def merge_vocab_argmax(val: torch.Tensor, gidx: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """Global greedy token of a vocab-parallel lm_head over a process group (the NCCL form of
+    ``mg_vocab_argmax``): ``val`` fp32 [b] and ``gidx`` int32 [b] are this rank's maximal logit and its global
+    column. All ranks' pairs are gathered; each row takes the largest value and, on ties, the lowest rank,
+    whose columns come first — torch.argmax's first maximal index over the whole row (``pytorch.py:153-155``).
+    NaN never wins, as in the local argmax kernel."""
+    import torch.distributed as dist
+    rec = torch.stack([val.contiguous().view(torch.int32), gidx.to(torch.int32)], 1)
+    parts = [torch.empty_like(rec) for _ in range(world)]
+    dist.all_gather(parts, rec, group=group)
+    allr = torch.stack(parts)                                   # [world, b, 2]
+    vals = allr[..., 0].contiguous().view(torch.float32)
+    vals = torch.where(torch.isnan(vals), torch.full_like(vals, float("-inf")), vals)
+    r = vals.argmax(0)                                          # first maximal rank
+    return allr[r, torch.arange(allr.shape[1], device=allr.device), 1]
+
+
 class WeightLoader:
     """Quantize full fp32 matrices on the device and keep this rank's shard.
 
     ``quantize`` maps an fp32 [N, K] weight to (int8 codes, fp32 scales) — the bit-exact device kernel
-    by default; ``pack`` repacks the kept codes into the tile-packed layout."""
+    by default; ``pack`` repacks the kept codes into the tile-packed layout. ``vocab_parallel`` keeps only
+    this rank's rows of lm_head (``vocab_bounds``); otherwise lm_head is replicated, as in the reference."""
 
-    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1, pack: bool = True, quantize=None):
+    def __init__(self, spec: ModelSpec, device, rank: int = 0, world: int = 1, pack: bool = True, quantize=None,
+                 vocab_parallel: bool = False):
         self.spec, self.device, self.rank, self.world, self.pack = spec, torch.device(device), rank, world, pack
+        self.vocab_parallel = bool(vocab_parallel) and world > 1
         self.quantize = quantize or K.quantize_rows_i8
         if spec.heads % world or spec.kv_heads % world:
             raise ValueError(f"{spec.heads} query / {spec.kv_heads} kv heads do not split over {world} ranks")
@@ -209,7 +239,12 @@ class WeightLoader:
             norm_w, norm_b = self.f32(state["model.norm.weight"]), None
             head = state.get("lm_head.weight", state["model.embed_tokens.weight"])
         lm_q, lm_s = self.quant(head)
-        w = ModelWeights(embed=embed, wpe=wpe, norm_w=norm_w, norm_b=norm_b, lm_q=lm_q, lm_s=lm_s, layers=layers)
+        lm_off = 0
+        if self.vocab_parallel:
+            lm_off, end = vocab_bounds(lm_q.shape[0], self.world)[self.rank]
+            lm_q, lm_s = lm_q[lm_off:end].contiguous(), lm_s[lm_off:end].contiguous()
+        w = ModelWeights(embed=embed, wpe=wpe, norm_w=norm_w, norm_b=norm_b, lm_q=lm_q, lm_s=lm_s, layers=layers,
+                         vocab_parallel=self.vocab_parallel, lm_offset=lm_off)
         if self.pack:
             w.lm_q = K.pack_weights(w.lm_q)
             for L in layers:
@@ -260,7 +295,12 @@ class DecodeEngine:
         self.q = torch.zeros((B, self.hq, self.D), dtype=torch.float32, device=dev)
         self.attn = torch.zeros((B, self.hq * self.D), dtype=torch.bfloat16, device=dev)
         self.act = torch.zeros((B, self.inter), dtype=torch.bfloat16, device=dev)
-        self.logits = torch.zeros((B, spec.vocab), dtype=torch.float32, device=dev)
+        # logits: the full vocab, or with a vocab-parallel lm_head this rank's columns in a buffer as wide as
+        # the widest shard (so the shards of all ranks gather into one [world, B, width] tensor)
+        self.vocab_parallel = weights.vocab_parallel
+        self.vocab_local = weights.lm_s.numel()
+        width = max(e - s_ for s_, e in vocab_bounds(spec.vocab, world)) if self.vocab_parallel else spec.vocab
+        self.logits = torch.zeros((B, width), dtype=torch.float32, device=dev)
         ws = max(K.attn_workspace_bytes(b, self.hq, self.hkv, self.D, max_blocks_per_seq, ns)
                  for b in {1, max_batch} for ns in {0, max_blocks_per_seq})
         self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)  # tickets start at zero
@@ -268,6 +308,7 @@ class DecodeEngine:
         self.stage = torch.zeros(4 * B + B * max_blocks_per_seq, dtype=torch.int32, pin_memory=True)
         self.stage_np = self.stage.numpy()
         self.graphs: dict = {}
+        self._pf: Optional[dict] = None  # prefill buffers, sized on first use
         # MG_STREAMK=1 runs the linears on the stream-K kernel (one wave of CTAs, equal weight bytes each;
         # it needs a zero-filled workspace for partial tiles); the default is the cluster split-K kernel,
         # which measured faster in the decode step (A/B in the same run)
@@ -360,15 +401,21 @@ class DecodeEngine:
         return n
 
     @staticmethod
-    def fused_allreduce_choice(group=None) -> bool:
-        """Whether the row-parallel linears reduce through the fused peer-memory push (MG_FUSED_AR unset or
-        not "0") or NCCL. Decided by the group's first rank and broadcast, so every rank takes the same path
-        even when their environments differ (a mix of the two paths would wait on pushes that never come)."""
-        want = [os.environ.get("MG_FUSED_AR", "1") != "0"]
+    def rank0_flag(name: str, group=None) -> bool:
+        """Environment switch ``name`` (on unless set to "0") as the group's first rank sees it, broadcast so
+        every rank takes the same path even when their environments differ (a mix of paths would wait on
+        pushes that never come)."""
+        want = [os.environ.get(name, "1") != "0"]
         import torch.distributed as dist
         src = dist.get_global_rank(group, 0) if group is not None else 0
         dist.broadcast_object_list(want, src=src, group=group)
         return bool(want[0])
+
+    @classmethod
+    def fused_allreduce_choice(cls, group=None) -> bool:
+        """Whether the row-parallel linears reduce through the fused peer-memory push (MG_FUSED_AR unset or
+        not "0") or NCCL."""
+        return cls.rank0_flag("MG_FUSED_AR", group)
 
     # ---- the step -----------------------------------------------------------------------------
     def _norm(self, h, w, b, x):
@@ -413,10 +460,7 @@ class DecodeEngine:
                 with P("decode_block", self.block_bytes(i, b)):
                     K.decode_block(a, self.block_ws, comm)
             if compute_logits:
-                with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, s.vocab)):
-                    K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32)
-                with P("argmax", b * s.vocab * 4):
-                    K.argmax_rows(self.logits[:b], out=self.next_tokens[:b])
+                self._head(b, P)
             return
         fused = self.comm is not None
         norm_kind = K.NORM_LAYER if s.family == "gpt2" else K.NORM_RMS
@@ -471,11 +515,125 @@ class DecodeEngine:
             if not fused:
                 with P("norm", b * H * 6):
                     self._norm(h, w.norm_w, w.norm_b, x)
-            with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, s.vocab)):
-                K.i8_linear(x, w.lm_q, w.lm_s, None, y=self.logits[:b], epilogue=K.EPI_STORE_F32,
-                            workspace=self.lin_ws)
-            with P("argmax", b * s.vocab * 4):
-                K.argmax_rows(self.logits[:b], out=self.next_tokens[:b])
+            self._head(b, P)
+
+    def _head(self, b: int, P) -> None:
+        """lm_head on x (this rank's rows of it when vocab-parallel) and the greedy token of every row."""
+        w, nl = self.w, self.vocab_local
+        lg = self.logits[:b, :nl]
+        with P("i8_linear", self.linear_bytes(w.lm_q, b, 4, nl)):
+            K.i8_linear(self.x[:b], w.lm_q, w.lm_s, None, y=lg, epilogue=K.EPI_STORE_F32, workspace=self.lin_ws)
+        with P("argmax", b * nl * 4):
+            if not self.vocab_parallel:
+                K.argmax_rows(lg, out=self.next_tokens[:b])
+            elif self.comm is not None:
+                K.vocab_argmax(self.comm, lg, w.lm_offset, out=self.next_tokens[:b])
+            else:
+                idx = K.argmax_rows(lg, out=self.next_tokens[:b])
+                val = lg.gather(1, idx.long()[:, None])[:, 0]
+                self.next_tokens[:b] = merge_vocab_argmax(val, idx + w.lm_offset, self.world, self.group)
+
+    def full_logits(self, b: int) -> torch.Tensor:
+        """fp32 [b, vocab] logits of the last step with logits, as a new tensor (every rank gets the whole
+        vocab: with a vocab-parallel lm_head the shards are gathered over the process group)."""
+        if not self.vocab_parallel:
+            return self.logits[:b].clone()
+        import torch.distributed as dist
+        mine = self.logits[:b].contiguous()
+        parts = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(parts, mine, group=self.group)
+        return torch.cat([p[:, :e - s_] for p, (s_, e) in zip(parts, vocab_bounds(self.spec.vocab, self.world))], 1)
+
+    # ---- prefill: many positions per launch ------------------------------------------------------
+    PREFILL_CHUNK = 64
+
+    def _prefill_buffers(self, rows: int, width: int) -> dict:
+        pf = self._pf
+        if pf is not None and pf["rows"] >= rows and pf["width"] >= width:
+            return pf
+        rows = max(rows, pf["rows"] if pf else 0)
+        width = max(width, pf["width"] if pf else 0)
+        self._pf = None
+        s, dev, H = self.spec, self.device, self.spec.hidden
+        n_in = 4 * rows + rows * width
+        pf = dict(rows=rows, width=width,
+                  h=torch.empty((rows, H), dtype=torch.float32, device=dev),
+                  x=torch.empty((rows, H), dtype=torch.bfloat16, device=dev),
+                  qkv=torch.empty((rows, (self.hq + 2 * self.hkv) * self.D), dtype=torch.float32, device=dev),
+                  q=torch.empty((rows, self.hq, self.D), dtype=torch.float32, device=dev),
+                  attn=torch.empty((rows, self.hq * self.D), dtype=torch.bfloat16, device=dev),
+                  act=torch.empty((rows, self.inter), dtype=torch.bfloat16, device=dev),
+                  inputs=torch.empty(n_in, dtype=torch.int32, device=dev),
+                  stage=torch.empty(n_in, dtype=torch.int32, pin_memory=True),
+                  ws=torch.zeros(16, dtype=torch.uint8, device=dev))
+        pf["stage_np"] = pf["stage"].numpy()
+        self._pf = pf
+        return pf
+
+    def prefill(self, ids, tables, start: int, end: int, compute_logits: bool = True,
+                chunk: Optional[int] = None) -> None:
+        """Positions [start, end) of ``b = len(ids)`` prompts, ``chunk`` positions of every prompt per pass
+        (the prefill form of ``PyTorchBackend.prefill``, ``pytorch.py:90-116``, which runs the whole prompt
+        in one forward): each linear runs once per pass on all b × chunk tokens (the tcgen05 kernel with
+        up to 256 tokens per tile), RoPE + K/V append writes every token's slot, and causal attention runs
+        per prompt on the decode kernel — the pass's queries share every block before the pass (read once
+        for all of them), and each query reads its own tail up to its position. ``ids[s][p]`` is token p of
+        prompt s; ``tables`` int32 [b, >= ceil(end/16)] already hold blocks for those positions. With
+        ``compute_logits``, writes logits[:b] and next_tokens[:b] of position end - 1."""
+        s, w = self.spec, self.w
+        b = len(ids)
+        C = int(chunk or self.PREFILL_CHUNK)
+        tab = np.asarray(tables, dtype=np.int32)
+        if tab.ndim != 2 or tab.shape[0] != b or tab.shape[1] * 16 < end or C < 1:
+            raise ValueError("prefill needs one table per prompt covering every position")
+        ids = np.asarray([list(r[start:end]) for r in ids], dtype=np.int32).reshape(b, end - start)
+        epi_mlp = K.EPI_GELU_BF16 if s.family == "gpt2" else K.EPI_SWIGLU_BF16
+        D = self.D
+        for c0 in range(start, end, C):
+            c1 = min(c0 + C, end)
+            L = c1 - c0
+            M, wc = b * L, (c1 + 15) // 16
+            pf = self._prefill_buffers(M, wc)
+            torch.cuda.current_stream(self.device).synchronize()  # the staging buffer may still be in flight
+            st = pf["stage_np"]
+            pos = np.arange(c0, c1, dtype=np.int32)
+            st[:M] = ids[:, c0 - start:c1 - start].ravel()
+            st[M:2 * M] = np.tile(pos, b)
+            st[2 * M:3 * M] = (tab[:, pos // 16] * 16 + pos % 16).ravel()
+            st[3 * M:4 * M] = np.tile(pos + 1, b)
+            st[4 * M:4 * M + M * wc] = np.repeat(tab[:, :wc], L, axis=0).ravel()
+            n = 4 * M + M * wc
+            inp = pf["inputs"]
+            inp[:n].copy_(pf["stage"][:n], non_blocking=True)
+            tok, posd, slots, ctx = (inp[i * M:(i + 1) * M] for i in range(4))
+            tabd = inp[4 * M:n].view(M, wc)
+            n_sh = c0 // 16 if L > 1 else 0
+            ws_need = K.attn_workspace_bytes(L, self.hq, self.hkv, D, wc, n_sh)
+            if ws_need > pf["ws"].numel():
+                pf["ws"] = torch.zeros(ws_need, dtype=torch.uint8, device=self.device)
+            h, x, qkv, q, attn, act = (pf[k][:M] for k in ("h", "x", "qkv", "q", "attn", "act"))
+            K.embed(tok, posd, w.embed, w.wpe, h)
+            for l, Lw in enumerate(w.layers):
+                self._norm(h, Lw.ln1_w, Lw.ln1_b, x)
+                K.i8_linear(x, Lw.qkv_q, Lw.qkv_s, Lw.qkv_b, y=qkv, epilogue=K.EPI_STORE_F32)
+                K.rope_kv_append(qkv, posd, self.cos_sin, slots, self.hq, self.hkv, D, self.pool.k[l],
+                                 self.pool.v[l], q_out=q)
+                for si in range(b):
+                    r = slice(si * L, (si + 1) * L)
+                    K.paged_decode_attn(q[r], self.pool.k[l], self.pool.v[l], tabd[r], ctx[r], self.scale,
+                                        n_shared_blocks=n_sh, out=attn[r], workspace=pf["ws"], validate=False)
+                bias_o = Lw.o_b if self.rank == 0 else None
+                row_parallel_residual(h, lambda y, e: K.i8_linear(attn, Lw.o_q, Lw.o_s, bias_o, y=y, epilogue=e),
+                                      self.rank, self.world, self.group)
+                self._norm(h, Lw.ln2_w, Lw.ln2_b, x)
+                K.i8_linear(x, Lw.gu_q, Lw.gu_s, Lw.gu_b, y=act, epilogue=epi_mlp)
+                bias_d = Lw.d_b if self.rank == 0 else None
+                row_parallel_residual(h, lambda y, e: K.i8_linear(act, Lw.d_q, Lw.d_s, bias_d, y=y, epilogue=e),
+                                      self.rank, self.world, self.group)
+            if compute_logits and c1 == end:
+                self.h[:b].copy_(h[L - 1::L])
+                self._norm(self.h[:b], w.norm_w, w.norm_b, self.x[:b])
+                self._head(b, lambda kind, nbytes: contextlib.nullcontext())
 
     def set_inputs(self, tokens, positions, slots, ctx, tables) -> int:
         """Stage one step's inputs in pinned host memory and copy them to the device input buffer in

@@ -315,6 +315,21 @@ def rowpar_reduce_norm(comm: Comm, h, bias, norm: int, w=None, b=None, eps: floa
     return x
 
 
+def vocab_argmax(comm: Comm, logits, offset: int, out=None):
+    """Global greedy argmax of logits split by columns across the ranks (this rank's fp32 shard
+    ``logits`` [m, n_local] holds global columns [offset, offset + n_local)): int32 [m], identical on
+    every rank, torch.argmax's first maximal index over the whole row. Every rank must call it at the
+    same point of the communicator's push / reduce sequence."""
+    _need(logits, torch.float32, "logits", contiguous=False)
+    m, n = logits.shape
+    if out is None:
+        out = torch.empty((m,), dtype=torch.int32, device=logits.device)
+    _lib.call("mg_vocab_argmax", comm.handle, _ptr(logits), m, n, logits.stride(0), int(offset), _ptr(out),
+              _stream())
+    _lib.LAUNCHES[0] += 1  # the local argmax, then the exchange and merge
+    return out
+
+
 # ---- persistent decode layer (mg_decode_block) -----------------------------------------------------
 BLK_O, BLK_MLP, BLK_N1, BLK_QKV = 1, 2, 4, 8
 BLOCK_MAX_TOKENS = 32

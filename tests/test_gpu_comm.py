@@ -4,7 +4,10 @@
   LayerNorm of it, against the fp64 oracle (partials travel as bf16: the contract's bf16 tolerance);
 * a missing peer: a world-2 communicator whose second rank never pushes — the reduce kernel's
   bounded wait gives up after about a second, records MG_ERR_TIMEOUT, and the host raises
-  TimeoutError; the context stays usable (a later world-1 reduce still works).
+  TimeoutError; the context stays usable (a later world-1 reduce still works);
+* the vocab-parallel greedy argmax (``mg_vocab_argmax``) at world 1 equals the local argmax kernel on
+  rows with exact ties, -inf and NaN entries, interleaved with row-parallel pushes of the same epoch
+  sequence; with a peer that never publishes it times out the same way.
 """
 
 import time
@@ -107,3 +110,52 @@ def test_decode_raises_when_a_peer_never_pushes():
         torch.cuda.synchronize()
         comm.close()
     test_world1_push_reduce_norm(1)  # the context is still healthy
+
+
+def _vocab_logits(m, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    lg = torch.randint(-4, 5, (m, n), generator=g).float()  # small integers: exact ties everywhere
+    lg[1] = float("-inf")
+    lg[2, ::5] = float("nan")
+    lg[3] = float("nan")
+    return lg.cuda()
+
+
+def test_world1_vocab_argmax_matches_local_argmax():
+    from microgen_b200 import kernels as K
+    m, k, n = 8, 256, 256
+    x, q, s, h0, bias, g, gb = _case(m, k, n, seed=3)
+    d = lambda a: torch.from_numpy(a).cuda()
+    comm = K.Comm(0, 1, m * n, exchange=lambda mine: [mine])
+    try:
+        h = d(h0.copy())
+        pw = K.pack_weights(d(q))
+        for rep in range(3):  # pushes and argmax exchanges share one epoch sequence and both sets
+            K.i8_linear_rowpar(x.cuda(), pw, d(s), comm)
+            K.rowpar_reduce_norm(comm, h, d(bias), 0)
+            lg = _vocab_logits(m, 1000 + rep, seed=rep)
+            want = K.argmax_rows(lg).cpu()
+            got = K.vocab_argmax(comm, lg, 0).cpu()
+            assert torch.equal(got, want), (got, want)
+            # a column slice with a row stride > its width, as the engine's shard buffer is
+            wide = torch.full((m, 1200), 7.0, device="cuda")
+            wide[:, :1000] = lg[:, :1000]
+            got2 = K.vocab_argmax(comm, wide[:, :1000], 0).cpu()
+            assert torch.equal(got2, K.argmax_rows(lg[:, :1000]).cpu())
+        K.check_device()
+    finally:
+        comm.close()
+
+
+def test_vocab_argmax_missing_peer_times_out():
+    from microgen_b200 import kernels as K
+    comm = K.Comm(0, 2, 4096, exchange=lambda mine: [mine, mine])
+    try:
+        t0 = time.time()
+        K.vocab_argmax(comm, _vocab_logits(4, 300, seed=1), 0)
+        with pytest.raises(TimeoutError):
+            K.check_device()
+        assert 0.5 < time.time() - t0 < 30
+    finally:
+        comm.close()
+    test_world1_vocab_argmax_matches_local_argmax()  # the context is still healthy

@@ -27,24 +27,32 @@ def _port():
 
 
 def _decode(be, prompts, forced=None):
-    """Greedy decode (or, with ``forced``, feed those tokens); returns (tokens, logits per step)."""
+    """Greedy decode (or, with ``forced``, feed those tokens); returns (tokens, logits per step, the
+    backend's greedy token per step). The greedy token comes from the step's device argmax (distributed
+    over the vocab shards at TP > 1); it must be the first maximal index of the returned logits."""
     logits, cache = be.prefill(torch.tensor(prompts))
-    toks, lgs = [], [logits.float().cpu().numpy()]
-    for i in range(N_NEW):
-        t = be.sample(logits) if forced is None else torch.tensor(forced[i], device="cuda")[:, None]
+    toks, lgs, greedy = [], [logits.float().cpu().numpy()], []
+    for i in range(N_NEW + 1):
+        gt = be.sample(logits)
+        greedy.append(gt[:, 0].cpu().tolist())
+        if i == N_NEW:
+            break
+        t = gt if forced is None else torch.tensor(forced[i], device="cuda")[:, None]
         toks.append(t[:, 0].cpu().tolist())
         logits, cache = be.decode(t, cache=cache)
         lgs.append(logits.float().cpu().numpy())
-    return toks, np.stack(lgs)
+    lgs = np.stack(lgs)
+    assert greedy == np.argmax(lgs, axis=-1).tolist()
+    return toks, lgs, greedy
 
 
-def _prompts():
+def _prompts(shape=SHAPE):
     from tests._hf_models import prompt_ids
-    shared = prompt_ids(SHAPE["vocab"], 32, seed=7)
-    return [shared + prompt_ids(SHAPE["vocab"], 9, seed=20 + i) for i in range(4)]
+    shared = prompt_ids(shape["vocab"], 32, seed=7)
+    return [shared + prompt_ids(shape["vocab"], 9, seed=20 + i) for i in range(4)]
 
 
-def _worker(rank, world, port, outdir, graph, forced, fused):
+def _worker(rank, world, port, outdir, graph, forced, fused, shape=SHAPE):
     import torch.distributed as dist
     os.environ["MG_FUSED_AR"] = "1" if fused else "0"
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -53,12 +61,13 @@ def _worker(rank, world, port, outdir, graph, forced, fused):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank))
-    model, _ = make_hf_model(SHAPE, seed=0)
+    model, _ = make_hf_model(shape, seed=0)
     be = B200TensorParallelBackend(world_size=world, group=dist.group.WORLD, max_batch=4, max_seq_len=128,
                                    use_cuda_graph=graph, free_list_seed=1)
     be.load_model("tiny", model_instance=model)
-    out = _decode(be, _prompts(), forced)
+    out = _decode(be, _prompts(shape), forced)
     assert (be.engine.comm is not None) == fused
+    assert be.engine.vocab_parallel and be.engine.vocab_local < shape["vocab"]
     be.engine.release_graphs()
     torch.save(out, os.path.join(outdir, f"r{rank}.pt"))
     torch.cuda.synchronize()
@@ -68,24 +77,34 @@ def _worker(rank, world, port, outdir, graph, forced, fused):
     dist.destroy_process_group()
 
 
+# an odd vocabulary: the last rank's lm_head shard is one row longer
+ODD_VOCAB = dict(SHAPE, vocab=1001)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("fused", [True, False], ids=["fused_push", "nccl"])
-@pytest.mark.parametrize("graph", [False, True])
-def test_tp2_matches_tp1(graph, fused):
+@pytest.mark.parametrize("fused,graph,shape", [(True, False, SHAPE), (True, True, SHAPE), (False, False, SHAPE),
+                                               (False, True, SHAPE), (True, True, ODD_VOCAB),
+                                               (False, True, ODD_VOCAB)],
+                         ids=["fused_push-eager", "fused_push-graph", "nccl-eager", "nccl-graph",
+                              "fused_push-graph-vocab1001", "nccl-graph-vocab1001"])
+def test_tp2_matches_tp1(graph, fused, shape):
+    """TP=2 with a vocab-parallel lm_head (each rank streams half of it; the greedy token is merged
+    across ranks on the device) against TP=1."""
     import torch.multiprocessing as mp
     from microgen_b200.backends import B200QuantizedBackend
     from tests._hf_models import make_hf_model
-    model, _ = make_hf_model(SHAPE, seed=0)
+    model, _ = make_hf_model(shape, seed=0)
     be = B200QuantizedBackend(max_batch=4, max_seq_len=128, free_list_seed=1, use_cuda_graph=graph)
     be.load_model("tiny", model_instance=model)
-    ref_toks, ref_lg = _decode(be, _prompts())
+    ref_toks, ref_lg, _ = _decode(be, _prompts(shape))
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks, fused), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks, fused, shape), nprocs=2, join=True)
         outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(2)]
     tol = 1e-2 + 2e-2 * np.abs(ref_lg)
     top2 = np.sort(ref_lg, axis=-1)[..., -2:]
     clear = (top2[..., 1] - top2[..., 0]) > 2 * tol.max(axis=-1)
-    for toks, lg in outs:
+    assert np.array_equal(outs[0][1], outs[1][1])  # every rank returns the same gathered logits
+    for toks, lg, _ in outs:
         assert toks == ref_toks  # teacher-forced inputs
         err = np.abs(lg - ref_lg)
         assert not (err > tol).any(), f"max err {err.max():.3e}"

@@ -70,6 +70,7 @@ def test_argument_errors_of_later_entry_points(lib):
     assert L.mg_rowpar_reduce_norm(None, None, None, 1, 128, 1, None, None, ctypes.c_float(1e-5), None,
                                    None) == bad
     assert L.mg_argmax_rows(None, 1, 8, 8, None, None) == bad
+    assert L.mg_vocab_argmax(None, None, 1, 8, 8, 0, None, None) == bad        # no communicator
     assert L.mg_argmax_rows(None, 1, 8, 4, None, None) == bad                   # ld < n
     assert L.mg_paged_decode_attn(None, None, None, 1, None, 1, None, 1, 24, 7, 128, 0, ctypes.c_float(1.0),
                                   None, None, 0, None) == bad                   # hq % hkv != 0

@@ -130,3 +130,75 @@ def test_tp_shards_reassemble_tp1_codes(world):
     rg = [_deinterleave(s["gu_q"]) for s in shards]
     assert torch.equal(torch.cat([g for g, _ in rg]), fg)
     assert torch.equal(torch.cat([u for _, u in rg]), fu)
+
+
+# ---- vocab-parallel lm_head -----------------------------------------------------------------------
+def _vocab_shard_worker(rank, world, port, outdir):
+    from microgen_b200.engine import WeightLoader
+    from microgen_b200.model_spec import spec_from_hf_config
+    from tests._hf_models import make_hf_model
+    _init(rank, world, port)
+    model, _ = make_hf_model(_shape(world), seed=0)
+    spec = spec_from_hf_config(model.config)
+    state = {k: v.detach() for k, v in model.state_dict().items()}
+    w = WeightLoader(spec, "cpu", rank, world, pack=False, quantize=_oracle_quantize,
+                     vocab_parallel=True).load(state)
+    torch.save({"lm_q": w.lm_q, "lm_s": w.lm_s, "off": w.lm_offset, "vp": w.vocab_parallel},
+               os.path.join(outdir, f"r{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_vocab_parallel_head_rows_reassemble(world):
+    """Each rank keeps lm_head rows [offset, offset + n) by the reference's split rule; in rank order the
+    shards are the world-size-1 codes and scales."""
+    from microgen_b200.engine import vocab_bounds
+    spec, full = _load(0, 1, _shape(world))
+    shards = _run(_vocab_shard_worker, world)
+    bounds = vocab_bounds(spec.vocab, world)
+    for s, (a, e) in zip(shards, bounds):
+        assert s["vp"] and s["off"] == a and s["lm_q"].shape[0] == e - a
+    assert torch.equal(torch.cat([s["lm_q"] for s in shards]), full.lm_q)
+    assert torch.equal(torch.cat([s["lm_s"] for s in shards]), full.lm_s)
+
+
+def test_vocab_bounds_split_rule():
+    from microgen_b200.engine import vocab_bounds
+    assert vocab_bounds(128256, 8) == [(r * 16032, (r + 1) * 16032) for r in range(8)]
+    assert vocab_bounds(50257, 2) == [(0, 25128), (25128, 50257)]   # remainder on the last rank
+    assert vocab_bounds(10, 3) == [(0, 3), (3, 6), (6, 10)]
+
+
+def _merge_worker(rank, world, port, outdir, vocab, seed):
+    from microgen_b200.engine import merge_vocab_argmax, vocab_bounds
+    _init(rank, world, port)
+    g = torch.Generator().manual_seed(seed)
+    b = 6
+    full = torch.randint(-3, 4, (b, vocab), generator=g).float()  # small integers: many exact ties
+    full[1] = float("-inf")                        # no finite value: torch.argmax gives 0
+    full[2, :] = 0.0
+    full[2, vocab - 1] = 5.0                       # the maximum in the last rank's shard
+    full[3, :] = float("nan")                      # NaN never wins; all NaN gives 0
+    full[4, ::3] = float("nan")
+    a, e = vocab_bounds(vocab, world)[rank]
+    shard = full[:, a:e]
+    clean = torch.where(torch.isnan(shard), torch.full_like(shard, float("-inf")), shard)
+    li = clean.argmax(1)                           # local first maximal column (NaN skipped)
+    val = clean.gather(1, li[:, None])[:, 0]
+    got = merge_vocab_argmax(val, (li + a).to(torch.int32), world, dist.group.WORLD)
+    torch.save({"got": got, "full": full}, os.path.join(outdir, f"r{rank}.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,vocab", [(2, 37), (3, 50), (4, 64)])
+def test_merge_vocab_argmax_matches_full_argmax(world, vocab):
+    """The NCCL-path merge of per-rank (max, global index) pairs equals torch.argmax over the whole row:
+    ties across shards go to the first index, -inf rows to 0, NaN ignored (all-NaN rows give 0)."""
+    outs = _run(_merge_worker, world, vocab, 5)
+    full = outs[0]["full"]
+    clean = torch.where(torch.isnan(full), torch.full_like(full, float("-inf")), full)
+    want = clean.argmax(1).to(torch.int32)
+    want[3] = 0
+    for o in outs:
+        assert torch.equal(o["got"], want), (o["got"], want)
