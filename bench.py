@@ -52,10 +52,18 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
     ap.add_argument("--sweep", default="", choices=["", "c4"],
                     help="c4: the isolated INT8-linear and paged-attention kernel sweep, one JSON line per case")
+    ap.add_argument("--kv", default="bf16", choices=["bf16", "int8"],
+                    help="KV cache storage: bf16 (the workload's default) or int8 codes with per-vector scales "
+                         "(the reference's quantize_kv option)")
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: KV filled with random values instead of a prefill, no window centering, "
                          "no probe / e2e / CPU legs")
     return ap.parse_args()
+
+
+def kv_vec_bytes(eng) -> int:
+    """Bytes of one K (or V) vector of one token and kv head in the pool: bf16, or int8 codes + an fp32 scale."""
+    return eng.D + 4 if eng.pool.quantize else 2 * eng.D
 
 
 def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps: int = 10) -> dict:
@@ -81,7 +89,7 @@ def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps:
     lin.append((eng.x[:b], w.lm_q, w.lm_s, None, eng.logits[:b, :eng.vocab_local], K.EPI_STORE_F32,
                 eng.linear_bytes(w.lm_q, b, 4, eng.vocab_local)))
     tab, ctx = eng.tables[:b], eng.ctx[:b]
-    attn_bytes = kv_tokens * eng.hkv * eng.D * 2 * 2 + b * eng.hq * eng.D * (4 + 2)
+    attn_bytes = kv_tokens * eng.hkv * kv_vec_bytes(eng) * 2 + b * eng.hq * eng.D * (4 + 2)
 
     def run_lin():
         for x, q, sc, bias, y, e, _ in lin:
@@ -109,7 +117,8 @@ def kernel_chains(eng, spec, b: int, n_shared_blocks: int, kv_tokens: int, reps:
     def run_attn():
         for l in range(len(w.layers)):
             K.paged_decode_attn(eng.q[:b], eng.pool.k[l], eng.pool.v[l], tab, ctx, eng.scale,
-                                n_shared_blocks=n_shared_blocks, out=eng.attn[:b], workspace=eng.workspace)
+                                n_shared_blocks=n_shared_blocks, out=eng.attn[:b], workspace=eng.workspace,
+                                **eng.pool.scales(l))
 
     out = {}
     families.append(("paged_attn", run_attn, len(w.layers), attn_bytes * len(w.layers)))
@@ -484,10 +493,17 @@ def random_fill(be, prompts, n_shared):
     else:
         cache.tables = [be.allocator.allocate_sequence(f"seq{i}", p) for i in range(b)]
     cache.n_shared_blocks = n_shared
-    g = torch.Generator(device=be.engine.pool.k.device).manual_seed(2)
-    for t in (be.engine.pool.k, be.engine.pool.v):
+    pool = be.engine.pool
+    g = torch.Generator(device=pool.k.device).manual_seed(2)
+    for t in (pool.k, pool.v):
         for l in range(t.shape[0]):
-            t[l].normal_(generator=g)
+            if pool.quantize:  # int8 codes; scales as a unit-normal vector would get
+                t[l].copy_(torch.randint(-127, 128, t[l].shape, generator=g, device=t.device, dtype=torch.int8))
+            else:
+                t[l].normal_(generator=g)
+    if pool.quantize:
+        pool.k_scale.fill_(3.0 / 127)
+        pool.v_scale.fill_(3.0 / 127)
     return cache
 
 
@@ -534,7 +550,8 @@ def main():
     n_shared = S // 16
     num_blocks = n_shared + B * (max_blocks - n_shared) + 16
 
-    kw = dict(max_batch=B, max_seq_len=max_seq, num_blocks=num_blocks, free_list_seed=0)
+    kw = dict(max_batch=B, max_seq_len=max_seq, num_blocks=num_blocks, free_list_seed=0,
+              quantize_kv=args.kv == "int8")
     be = (B200TensorParallelBackend(world_size=world, group=group, **kw) if world > 1
           else B200QuantizedBackend(**kw))
     t0 = time.time()
@@ -676,7 +693,7 @@ def main():
                 "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": hbm_kind,
                 "algorithmic_bytes_per_launch": chains[dom]["bytes_per_launch"],
                 "us_per_launch": chains[dom]["us_per_launch"], "timing": chains[dom]["timing"]}
-    step_bytes = eng.w.int8_bytes() + kv_tokens * eng.hkv * spec.head_dim * 2 * 2 * spec.layers
+    step_bytes = eng.w.int8_bytes() + kv_tokens * eng.hkv * kv_vec_bytes(eng) * 2 * spec.layers
     step_roofline = {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms / 1e3) / 1e9, 1),
                      "frac": round(step_bytes / (ms / 1e3) / 1e9 / hbm, 4)}
 
@@ -730,7 +747,7 @@ def main():
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": Kst,
         "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 weights x bf16 activations, fp32 accumulate", "data": "synthetic",
-        "config": workload_config(args.workload, wl, world),
+        "config": dict(workload_config(args.workload, wl, world), **({"kv": "int8"} if args.kv == "int8" else {})),
         "setup": {"l2": "working set per step >> L2 (no flush needed)", "cuda_graph": True,
                   "row_parallel_reduce": reduce_kind,
                   "linear_kernel": ("persistent layer kernel (decode_block) + cluster split-K lm_head"

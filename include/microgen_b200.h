@@ -15,6 +15,8 @@
  *   microgen/backends/parallel.py:65-81    RowParallelLinear.forward (+sum)  -> mg_i8_linear_packed_rowpar +
  *                                                                            mg_rowpar_reduce_norm
  *   microgen/runtime/kv_cache.py:76-127    KVCacheState.update (torch.cat)   -> mg_rope_kv_append (paged slot write)
+ *   microgen/runtime/kv_cache.py:30-40     INT8 KV (quantize_kv)             -> mg_rope_kv_append_kv8 +
+ *                                                                            mg_paged_decode_attn_kv8
  *   transformers sdpa_attention_forward    decode SDPA over the cache        -> mg_paged_decode_attn
  *   microgen/backends/pytorch.py:153-155   greedy torch.argmax               -> mg_argmax_rows
  */
@@ -226,6 +228,24 @@ int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool,
                          const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b, int hq,
                          int hkv, int d, int n_shared_blocks, float scale, void* out, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* ---- paged INT8 KV (kv_cache.py:30-40, 114-120: KVCacheState with quantize_kv) ------------------
+ * Pools int8 [num_blocks, hkv, 16, d] and one fp32 scale per (block, kv head, token) vector in
+ * k_scales / v_scales [num_blocks, hkv, 16] (16-byte aligned). mg_rope_kv_append_kv8: as
+ * mg_rope_kv_append, then each K and V vector of d values x is stored as s = max(max|x| / 127, 1e-8),
+ * code = clamp(round_half_even(x / s), -128, 127) — the reference's _quantize_tensor over head_dim.
+ * mg_paged_decode_attn_kv8: as mg_paged_decode_attn over those pools, with K and V the codes times their
+ * scales (the codes enter the tensor cores exactly; the scales multiply the scores and the probabilities).
+ * Workspace bytes as mg_paged_attn_workspace_bytes. The step's own token is read back quantized, where the
+ * reference attends to it before quantizing. */
+int mg_rope_kv_append_kv8(const float* qkv, int64_t ld_qkv, const int32_t* positions, const float* cos_sin,
+                          int max_pos, const int32_t* slot_mapping, int b, int hq, int hkv, int d, float* q_out,
+                          int8_t* k_pool, int8_t* v_pool, float* k_scales, float* v_scales, int64_t num_blocks,
+                          void* stream);
+int mg_paged_decode_attn_kv8(const float* q, const int8_t* k_pool, const int8_t* v_pool, const float* k_scales,
+                             const float* v_scales, int64_t num_blocks, const int32_t* block_tables, int max_blocks,
+                             const int32_t* ctx_lens, int b, int hq, int hkv, int d, int n_shared_blocks,
+                             float scale, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free paged decode attention. No counterpart in the reference: it exists for callers that
  * cannot allocate device memory themselves — a host binding that only receives pointers from another

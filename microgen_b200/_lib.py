@@ -50,8 +50,10 @@ SIGNATURES = {
     "mg_i8_linear_packed_rowpar": [_p, _i64, _i64, _i64, _p, _p, _i64, _p, _i, _p],
     "mg_rowpar_reduce_norm": [_p, _p, _p, _i, _i, _i, _p, _p, _f, _p, _p],
     "mg_rope_kv_append": [_p, _i64, _p, _p, _i, _p, _i, _i, _i, _i, _p, _p, _p, _i64, _p],
+    "mg_rope_kv_append_kv8": [_p, _i64, _p, _p, _i, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _i64, _p],
     "mg_paged_attn_workspace_bytes": [_i, _i, _i, _i, _i, _i, C.POINTER(C.c_size_t)],
     "mg_paged_decode_attn": [_p, _p, _p, _i64, _p, _i, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p],
+    "mg_paged_decode_attn_kv8": [_p, _p, _p, _p, _p, _i64, _p, _i, _p, _i, _i, _i, _i, _i, _f, _p, _p, _sz, _p],
     "mg_paged_decode_attn_noalloc": [_p, _p, _p, _i64, _p, _i, _p, _i, _i, _i, _i, _i, _f, _p, _p],
     "mg_embed": [_p, _p, _p, _p, _i, _i, _i64, _i, _p, _p],
     "mg_rmsnorm": [_p, _p, _i, _i, _f, _p, _p],
@@ -73,7 +75,8 @@ LAUNCHING = {"mg_quantize_rows_i8", "mg_i8_linear", "mg_i8_linear_simt", "mg_i8_
              "mg_i8_linear_packed_rowpar", "mg_rowpar_reduce_norm", "mg_i8_linear_packed_sk",
              "mg_i8_linear_packed_rowpar_sk",
              "mg_paged_decode_attn", "mg_embed", "mg_rmsnorm", "mg_layernorm", "mg_argmax_rows",
-             "mg_decode_advance", "mg_decode_block", "mg_vocab_argmax"}
+             "mg_decode_advance", "mg_decode_block", "mg_vocab_argmax", "mg_rope_kv_append_kv8",
+             "mg_paged_decode_attn_kv8"}
 LAUNCHES = [0]  # kernels launched (or captured) through call() in this process
 
 _lock = threading.Lock()

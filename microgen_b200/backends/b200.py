@@ -102,7 +102,7 @@ class B200QuantizedBackend:
     def __init__(self, device=None, quant_type: str = "int8", max_batch: int = 64, max_seq_len: int = 4096,
                  num_blocks: Optional[int] = None, use_cuda_graph: bool = True, free_list_seed: Optional[int] = None,
                  world_size: int = 1, group=None, device_check_every: int = 1,
-                 prefix_cache_capacity: int = 0, prefill_chunk: int = 64) -> None:
+                 prefix_cache_capacity: int = 0, prefill_chunk: int = 64, quantize_kv: bool = False) -> None:
         """``device_check_every``: after every that many ``decode`` calls, read the library's device error
         word (one stream synchronisation) and raise — TimeoutError when a bounded wait gave up (a peer
         rank that never pushed its row-parallel partial), RuntimeError for a failed device-side check —
@@ -111,6 +111,10 @@ class B200QuantizedBackend:
         ``prefix_cache_capacity`` > 0 keeps a block-level prefix cache (``PagedPrefixCache``) of that many
         entries: a prefill whose prompts start with a cached run of whole blocks shares those blocks instead
         of recomputing them, and every prefill's whole-block common prefix is cached for later calls.
+
+        ``quantize_kv``: keep K/V as int8 codes with one fp32 scale per (token, kv head) vector, as the
+        reference's ``KVCacheState(quantize_kv=True)`` does (``kv_cache.py:30-40, 114-120``): half the KV bytes
+        per decode step.
 
         ``prefill_chunk``: prompt positions per prefill pass (every prompt of the batch at once, the
         linears on all those tokens per launch); 0 runs the prompt through the decode step one position at
@@ -133,6 +137,7 @@ class B200QuantizedBackend:
         self._greedy = None
         self.prefix_cache_capacity = int(prefix_cache_capacity)
         self.prefill_chunk = max(0, int(prefill_chunk))
+        self.quantize_kv = bool(quantize_kv)
         self.prefix_cache: Optional[PagedPrefixCache] = None
         self.rank = torch.distributed.get_rank(group) if world_size > 1 else 0
         self.engine: Optional[DecodeEngine] = None
@@ -163,7 +168,7 @@ class B200QuantizedBackend:
             max_blocks = (self.max_seq_len + BLOCK - 1) // BLOCK
             self.engine = DecodeEngine(spec, weights, dev, self.max_batch, self.num_blocks, max_blocks,
                                        rank=self.rank, world=self.world_size, group=self.group,
-                                       max_pos=self.max_seq_len)
+                                       max_pos=self.max_seq_len, quantize_kv=self.quantize_kv)
         self.allocator = PagedKVCacheAllocator(num_blocks=self.num_blocks, block_size=BLOCK)
         if self.free_list_seed is not None:
             self.allocator.shuffle_free_list(self.free_list_seed)

@@ -213,6 +213,72 @@ __global__ void rope_kv_append_kernel(const float* __restrict__ qkv, int64_t ld_
   dst[j + half] = __float2bfloat16_rn(b);
 }
 
+// INT8 paged KV: the same rotation, then each K and V vector (one token, one kv head) is quantized as
+// KVCacheState stores it with quantize_kv (kv_cache.py:30-35, 114-120): s = max(max|x| / 127, 1e-8),
+// code = clamp(round_half_even(x / s), -128, 127) — int8 codes into the pools, s into the scale arrays
+// (fp32 [num_blocks, hkv, 16]) at the same slot. Every thread of a CTA takes part in the vector's max.
+__global__ void rope_kv_append_kv8_kernel(const float* __restrict__ qkv, int64_t ld_qkv,
+                                          const int32_t* __restrict__ positions, const float* __restrict__ cos_sin,
+                                          int max_pos, const int32_t* __restrict__ slots, int hq, int hkv, int d,
+                                          float* __restrict__ q_out, int8_t* __restrict__ k_pool,
+                                          int8_t* __restrict__ v_pool, float* __restrict__ k_scales,
+                                          float* __restrict__ v_scales, int64_t num_blocks) {
+  __shared__ float red[32];
+  griddep_launch();
+  griddep_wait();
+  const int i = blockIdx.x, hd = blockIdx.y, j = threadIdx.x;
+  const int half = d >> 1;
+  const bool act = j < half;
+  const float* src = qkv + (int64_t)i * ld_qkv + (int64_t)hd * d;
+  float a = act ? src[j] : 0.f, b = act ? src[j + half] : 0.f;
+  if (hd < hq + hkv && cos_sin) {
+    const int pos = positions[i];
+    if (pos < 0 || pos >= max_pos) {
+      if (j == 0) mg_record_error(MG_ERR_DEVICE, 200);
+      return;
+    }
+    if (act) {
+      const float* cs = cos_sin + (int64_t)pos * d;
+      const float c = cs[j], sn = cs[half + j];
+      const float ra = a * c - b * sn;
+      const float rb = b * c + a * sn;
+      a = ra;
+      b = rb;
+    }
+  }
+  if (hd < hq) {
+    if (act) {
+      float* dst = q_out + ((int64_t)i * hq + hd) * d;
+      dst[j] = a;
+      dst[j + half] = b;
+    }
+    return;
+  }
+  const int slot = slots[i];
+  const int64_t blk = slot >> 4;
+  if (slot < 0 || blk >= num_blocks) {
+    if (j == 0) mg_record_error(MG_ERR_DEVICE, 201);
+    return;
+  }
+  float mx = fmaxf(fabsf(a), fabsf(b));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((j & 31) == 0) red[j >> 5] = mx;
+  __syncthreads();
+  mx = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+  const float sc = fmaxf(__fdiv_rn(mx, 127.f), 1e-8f);
+  const bool is_k = hd < hq + hkv;
+  const int kh = is_k ? hd - hq : hd - hq - hkv;
+  const int64_t row = (blk * hkv + kh) * 16 + (slot & 15);
+  if (act) {
+    int8_t* dst = (is_k ? k_pool : v_pool) + row * (int64_t)d;
+    dst[j] = (int8_t)fminf(fmaxf(rintf(__fdiv_rn(a, sc)), -128.f), 127.f);
+    dst[j + half] = (int8_t)fminf(fmaxf(rintf(__fdiv_rn(b, sc)), -128.f), 127.f);
+  }
+  if (j == 0) (is_k ? k_scales : v_scales)[row] = sc;
+}
+
 // torch.argmax semantics: the first index holding the maximum. A row is split over a cluster of
 // kArgSplit CTAs (contiguous chunks, float4 loads where the row is 16-byte aligned); CTA 0 of the
 // cluster merges the chunk results through distributed shared memory, smaller index on ties.
@@ -372,6 +438,24 @@ extern "C" int mg_rope_kv_append(const float* qkv, int64_t ld_qkv, const int32_t
   MG_CUDA_TRY(mg_launch(rope_kv_append_kernel, grid, dim3((d / 2 + 31) / 32 * 32), 0, mg_stream(stream), 1, qkv,
                         ld_qkv, positions, cos_sin, max_pos, slot_mapping, hq, hkv, d, q_out,
                         static_cast<__nv_bfloat16*>(k_pool), static_cast<__nv_bfloat16*>(v_pool), num_blocks));
+  MG_LAUNCH_CHECK();
+  return MG_OK;
+}
+
+extern "C" int mg_rope_kv_append_kv8(const float* qkv, int64_t ld_qkv, const int32_t* positions,
+                                     const float* cos_sin, int max_pos, const int32_t* slot_mapping, int b, int hq,
+                                     int hkv, int d, float* q_out, int8_t* k_pool, int8_t* v_pool, float* k_scales,
+                                     float* v_scales, int64_t num_blocks, void* stream) {
+  if (b < 0 || hq <= 0 || hkv <= 0 || hq % hkv || d <= 0 || (d & 1) || !qkv || !slot_mapping || !q_out || !k_pool ||
+      !v_pool || !k_scales || !v_scales || num_blocks <= 0 || ld_qkv < (int64_t)(hq + 2 * hkv) * d ||
+      (cos_sin && (!positions || max_pos <= 0)))
+    return MG_ERR_INVALID_ARG;
+  if (b == 0) return MG_OK;
+  if (d > 2 * 1024) return MG_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)b, (unsigned)(hq + 2 * hkv));
+  MG_CUDA_TRY(mg_launch(rope_kv_append_kv8_kernel, grid, dim3((d / 2 + 31) / 32 * 32), 0, mg_stream(stream), 1, qkv,
+                        ld_qkv, positions, cos_sin, max_pos, slot_mapping, hq, hkv, d, q_out, k_pool, v_pool,
+                        k_scales, v_scales, num_blocks));
   MG_LAUNCH_CHECK();
   return MG_OK;
 }

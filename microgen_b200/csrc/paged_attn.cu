@@ -19,6 +19,13 @@
 // Each CTA leaves (m, l, unnormalised O) per query head in a workspace slot, and a combine
 // kernel merges the slots (log-sum-exp). With no shared prefix and one split the private CTA
 // writes the normalised output itself.
+//
+// INT8 KV (Q8): pools are int8 [num_blocks, hkv, 16, d] with one fp32 scale per (block, kv head,
+// token) vector for K and for V. A stage holds the int8 K and V tiles (TMA, no swizzle) and their 16 + 16
+// scales (bulk copies). The consumer converts the integer codes exactly to bf16 (a private CTA's warp into
+// its own tile buffer, the shared CTA's warps together into a double buffer) and applies the scales
+// outside the MMAs: each score is multiplied by its key's scale, and each probability by its value's scale
+// before the PV product (the softmax sum uses the unscaled probabilities).
 #include "common.cuh"
 
 namespace {
@@ -30,16 +37,22 @@ constexpr int kStages = 8;               // KV ring stages (a multiple of kCons)
 constexpr int kChunk = 8;                // shared-prefix blocks per shared CTA (<= kStages)
 static_assert(kStages % kCons == 0 && kChunk <= kStages, "ring layout");
 
-template <int D>
+template <int D, bool Q8 = false>
 struct AttnCfg {
-  static constexpr int kTileBytes = 16 * D * 2;          // K (or V) of one block and kv head
-  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kBf16Tile = 16 * D * 2;                // bf16 K (or V) of one block and kv head
+  static constexpr int kTileBytes = Q8 ? 16 * D : kBf16Tile;  // as stored in the pool
+  static constexpr int kScaleOff = 2 * kTileBytes;            // Q8: 16 K scales, then 16 V scales
+  static constexpr int kStageBytes = 2 * kTileBytes + (Q8 ? 128 : 0);
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kMergeBytes = kCons * 16 * (D + 2) * 4;
   static constexpr int kMain = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
-  static constexpr int kBarOffset = (kMain + 7) / 8 * 8;
+  // Q8: converted bf16 tiles + their 32 scales, one buffer per consumer warp (the shared CTA uses two)
+  static constexpr int kBufBytes = 2 * kBf16Tile + 128;
+  static constexpr int kBufOffset = (kMain + 127) / 128 * 128;
+  static constexpr int kBufTotal = Q8 ? kCons * kBufBytes : 0;
+  static constexpr int kBarOffset = (kBufOffset + kBufTotal + 7) / 8 * 8;
   static constexpr int kSmem = kBarOffset + (2 * kStages + 1) * 8 + 1024;  // + 1 KB alignment slack
-  static constexpr int kBoxCols = D >= 64 ? 64 : D;       // one TMA box row = 128 B (64 B for d = 32)
+  static constexpr int kBoxCols = D >= 64 ? 64 : D;       // one bf16 TMA box row = 128 B (64 B for d = 32)
 };
 
 // Byte offset of (row, col) in a tile. d >= 64: halves of 64 columns, each 16 rows x 128 B with the
@@ -75,16 +88,57 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// TMA loads of the K and V tiles of (block phys, kv head h) into one ring stage.
-template <int D>
+// TMA loads of the K and V tiles of (block phys, kv head h) into one ring stage; with Q8 the int8
+// tiles (one box of 16 rows x d bytes each) and the tiles' K and V scales (64 bytes each).
+template <int D, bool Q8 = false>
 __device__ __forceinline__ void load_stage(uint8_t* st, const CUtensorMap* tk, const CUtensorMap* tv, uint64_t* bar,
-                                           int row) {
-  constexpr int T = AttnCfg<D>::kTileBytes;
-  mbar_arrive_expect_tx(bar, AttnCfg<D>::kStageBytes);
+                                           int row, const float* k_scales = nullptr,
+                                           const float* v_scales = nullptr) {
+  using C = AttnCfg<D, Q8>;
+  constexpr int T = C::kTileBytes;
+  mbar_arrive_expect_tx(bar, C::kStageBytes);
+  if constexpr (Q8) {
+    tma_load_2d(st, tk, bar, 0, row);
+    tma_load_2d(st + T, tv, bar, 0, row);
+    bulk_load_smem(st + C::kScaleOff, k_scales + row, 64, bar);
+    bulk_load_smem(st + C::kScaleOff + 64, v_scales + row, 64, bar);
+  } else {
 #pragma unroll
-  for (int c = 0; c < D; c += AttnCfg<D>::kBoxCols) {
-    tma_load_2d(st + c * 32, tk, bar, c, row);  // 16 rows x 128 B = 2 KB per 64 columns
-    tma_load_2d(st + T + c * 32, tv, bar, c, row);
+    for (int c = 0; c < D; c += C::kBoxCols) {
+      tma_load_2d(st + c * 32, tk, bar, c, row);  // 16 rows x 128 B = 2 KB per 64 columns
+      tma_load_2d(st + T + c * 32, tv, bar, c, row);
+    }
+  }
+}
+
+// Q8: the int8 K and V tiles of a stage -> exact bf16 integers in the swizzled tile layout of the bf16
+// path at dst (K, then V), and the stage's scales after them (V scales of tokens >= valid become 0, so a
+// zero probability never meets a stale scale). Threads t, t + n, ... of the n taking part.
+template <int D>
+__device__ __forceinline__ void convert_stage(const uint8_t* st, uint8_t* dst, int valid, int t, int n) {
+  using C = AttnCfg<D, true>;
+  constexpr int kChunks = 16 * D / 16;  // 16-byte chunks per int8 tile
+  const uint32_t dk = smem_u32(dst);
+  for (int c = t; c < 2 * kChunks; c += n) {
+    const int kv = c >= kChunks, cc = c - kv * kChunks;
+    const int row = cc / (D / 16), col = (cc % (D / 16)) * 16;
+    const uint4 w = *reinterpret_cast<const uint4*>(st + kv * C::kTileBytes + cc * 16);
+    uint32_t r[8];
+    i8x4_to_bf16x4(w.x, r[0], r[1]);
+    i8x4_to_bf16x4(w.y, r[2], r[3]);
+    i8x4_to_bf16x4(w.z, r[4], r[5]);
+    i8x4_to_bf16x4(w.w, r[6], r[7]);
+    const uint32_t base = dk + kv * C::kBf16Tile;
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + swz<D>(row, col)), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + swz<D>(row, col + 8)), "r"(r[4]), "r"(r[5]),
+                 "r"(r[6]), "r"(r[7])
+                 : "memory");
+  }
+  for (int j = t; j < 32; j += n) {
+    const float v = reinterpret_cast<const float*>(st + C::kScaleOff)[j];
+    reinterpret_cast<float*>(dst + 2 * C::kBf16Tile)[j] = (j >= 16 && j - 16 >= valid) ? 0.f : v;
   }
 }
 
@@ -103,7 +157,8 @@ __device__ __forceinline__ void zero_v_tail(uint32_t vs, int valid, int lane) {
 // Online-softmax update of one 16-row query tile with one 16-token KV tile.
 template <int D>
 __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uint32_t ks, uint32_t vs, int valid,
-                                            float (&o)[D / 8][4], float (&m)[2], float (&l)[2], int lane) {
+                                            float (&o)[D / 8][4], float (&m)[2], float (&l)[2], int lane,
+                                            const float* sc = nullptr) {
   float s[2][4];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -119,6 +174,12 @@ __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uin
     mma_bf16(s[1], qa[kk], b2, b3);
   }
   const int tq = (lane & 3) * 2;
+  if (sc) {  // Q8: key scales (score column nt * 8 + tq + (c & 1) is that key)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[nt][c] *= sc[nt * 8 + tq + (c & 1)];
+  }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -151,6 +212,12 @@ __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uin
     o[dn][2] *= alpha[1];
     o[dn][3] *= alpha[1];
   }
+  if (sc) {  // Q8: value scales fold into the probabilities
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[nt][c] *= sc[16 + nt * 8 + tq + (c & 1)];
+  }
   uint32_t pa[4];
   pa[0] = pack_bf16x2(s[0][0], s[0][1]);
   pa[1] = pack_bf16x2(s[0][2], s[0][3]);
@@ -173,7 +240,8 @@ __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uin
 // m, l: running max / sum of heads 2t and 2t+1 (t = lane % 4).
 template <int D>
 __device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], uint32_t ks, uint32_t vs, int valid,
-                                              float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane) {
+                                              float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane,
+                                              const float* sc = nullptr) {
   const int g = lane >> 2, t = lane & 3;
   float s[4] = {0.f, 0.f, 0.f, 0.f};
   const int arow = lane & 15, acol = (lane >> 4) * 8;
@@ -182,6 +250,13 @@ __device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], u
     uint32_t a[4];
     ldsm_x4(ks + swz<D>(arow, kk * 16 + acol), a[0], a[1], a[2], a[3]);
     mma_bf16(s, a, qb[kk][0], qb[kk][1]);
+  }
+  if (sc) {  // Q8: key scales (rows g and g + 8 are keys)
+    const float k0 = sc[g], k1 = sc[g + 8];
+    s[0] *= k0;
+    s[1] *= k0;
+    s[2] *= k1;
+    s[3] *= k1;
   }
   if (g >= valid) s[0] = s[1] = -INFINITY;
   if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
@@ -209,6 +284,13 @@ __device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], u
   }
   // Pᵀ as the B operand (k = tokens, n = heads): thread (g, t) needs tokens 2t, 2t+1, 2t+8, 2t+9 of
   // head g, held (as halves of packed head pairs) by the threads of rows 2t and 2t+1.
+  if (sc) {  // Q8: value scales fold into the probabilities
+    const float v0 = sc[16 + g], v1 = sc[16 + g + 8];
+    s[0] *= v0;
+    s[1] *= v0;
+    s[2] *= v1;
+    s[3] *= v1;
+  }
   const uint32_t lo = pack_bf16x2(s[0], s[1]), hi = pack_bf16x2(s[2], s[3]);
   const int src = 8 * t + (g >> 1);
   const uint32_t x = __shfl_sync(0xffffffffu, lo, src), y = __shfl_sync(0xffffffffu, lo, src + 4);
@@ -279,12 +361,14 @@ struct AttnParams {
   float* ws_o;  // [b, hq, nslots, d]
   float* ws_ml; // [b, hq, nslots, 2]
   bool direct;  // private CTA writes the final output
+  const float* k_scales;  // Q8: fp32 [num_blocks * hkv * 16]
+  const float* v_scales;
 };
 
-template <int D, bool T>
+template <int D, bool T, bool Q8>
 __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, int pair, int sp,
                             uint8_t* smem, uint64_t* full, uint64_t* empty) {
-  using C = AttnCfg<D>;
+  using C = AttnCfg<D, Q8>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = pair / p.hkv, h = pair % p.hkv;
   const int b0 = p.n_shared + sp * p.bps;
@@ -326,7 +410,9 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
       if (lane == 0) {
         const int s = i % kStages;
         if (i >= kStages) ok = mbar_wait(&empty[s], ((i / kStages) - 1) & 1, 411);
-        if (ok) load_stage<D>(smem + s * C::kStageBytes, tk, tv, &full[s], (int)((phys * p.hkv + h) * 16));
+        if (ok)
+          load_stage<D, Q8>(smem + s * C::kStageBytes, tk, tv, &full[s], (int)((phys * p.hkv + h) * 16), p.k_scales,
+                            p.v_scales);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
@@ -341,17 +427,33 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
     for (int i = warp; i < ntiles; i += kCons) {
       const int s = i % kStages;
       if (!mbar_wait(&full[s], (i / kStages) & 1, 410)) break;
-      const uint32_t ks = smem_u32(smem + s * C::kStageBytes), vs = ks + C::kTileBytes;
       const int valid = min(16, ctx - (b0 + i) * 16);
-      if (valid < 16) zero_v_tail<D>(vs, valid, lane);
-      if constexpr (T) {
-        attend_tile_t<D>(qa, ks, vs, valid, o, m, l, lane);
+      if constexpr (Q8) {
+        // the stage's codes become this warp's bf16 tile; the stage is released once they are stored
+        uint8_t* wb = smem + C::kBufOffset + warp * C::kBufBytes;
+        convert_stage<D>(smem + s * C::kStageBytes, wb, valid, lane, 32);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        const uint32_t ks = smem_u32(wb), vs = ks + C::kBf16Tile;
+        const float* sc = reinterpret_cast<const float*>(wb + 2 * C::kBf16Tile);
+        if constexpr (T) {
+          attend_tile_t<D>(qa, ks, vs, valid, o, m, l, lane, sc);
+        } else {
+          attend_tile<D>(qa, ks, vs, valid, o, m, l, lane, sc);
+        }
+        __syncwarp();  // every lane is done with the buffer before the next conversion
       } else {
-        attend_tile<D>(qa, ks, vs, valid, o, m, l, lane);
+        const uint32_t ks = smem_u32(smem + s * C::kStageBytes), vs = ks + C::kTileBytes;
+        if (valid < 16) zero_v_tail<D>(vs, valid, lane);
+        if constexpr (T) {
+          attend_tile_t<D>(qa, ks, vs, valid, o, m, l, lane);
+        } else {
+          attend_tile<D>(qa, ks, vs, valid, o, m, l, lane);
+        }
+        if (valid < 16) fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      if (valid < 16) fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
     }
   }
   __syncthreads();  // every tile consumed: the ring is free for the merge
@@ -417,10 +519,10 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
   }
 }
 
-template <int D>
+template <int D, bool Q8>
 __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUtensorMap* tv, int h, int chunk,
                            int rg, uint8_t* smem, uint64_t* full) {
-  using C = AttnCfg<D>;
+  using C = AttnCfg<D, Q8>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int blk0 = chunk * kChunk;
   const int nb = min(kChunk, p.n_shared - blk0);
@@ -433,13 +535,16 @@ __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUt
     }
     for (int i = 0; i < nb; ++i) {
       const int64_t ph = __shfl_sync(0xffffffffu, phys, i);
-      if (lane == 0) load_stage<D>(smem + i * C::kStageBytes, tk, tv, &full[i], (int)((ph * p.hkv + h) * 16));
+      if (lane == 0)
+        load_stage<D, Q8>(smem + i * C::kStageBytes, tk, tv, &full[i], (int)((ph * p.hkv + h) * 16), p.k_scales,
+                          p.v_scales);
     }
     return;
   }
   const int rows = p.b * p.group;
   const int t = rg * kCons + warp;  // this warp's 16-row query tile
-  if (t * 16 >= rows) return;
+  // Q8: every consumer warp converts its share of each stage, so warps without a row tile stay
+  if (t * 16 >= rows && !Q8) return;
   const int c = (lane & 3) * 2;
   const int r0 = t * 16 + (lane >> 2), r1 = r0 + 8;
   const int s0 = r0 < rows ? r0 / p.group : -1, s1 = r1 < rows ? r1 / p.group : -1;
@@ -449,15 +554,40 @@ __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUt
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  for (int i = 0; i < nb; ++i) {
-    if (!mbar_wait(&full[i], 0, 412)) {
-      // timed out (MG_ERR_TIMEOUT recorded): leave an empty state so the merge gives this slot no weight
+  if constexpr (Q8) {
+    // Stage i is converted by all consumer warps into buffer i % 2, then each warp runs its rows against
+    // it. One consumer barrier per stage: a warp past the barrier of stage i + 1 has finished stage i, so
+    // buffer i % 2 is free again when stage i + 2 is converted. Every warp takes every barrier, also after
+    // a timed-out wait (the slot is then reported empty).
+    bool bad = false;
+    for (int i = 0; i < nb; ++i) {
+      const bool ok = mbar_wait(&full[i], 0, 412);
+      bad |= !ok;
+      uint8_t* buf = smem + C::kBufOffset + (i & 1) * C::kBufBytes;
+      if (ok) convert_stage<D>(smem + i * C::kStageBytes, buf, 16, threadIdx.x, kCons * 32);
+      asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
+      if (!bad && t * 16 < rows) {
+        const uint32_t ks = smem_u32(buf);
+        attend_tile<D>(qa, ks, ks + C::kBf16Tile, 16, o, m, l, lane,
+                       reinterpret_cast<const float*>(buf + 2 * C::kBf16Tile));
+      }
+    }
+    if (t * 16 >= rows) return;
+    if (bad) {
       m[0] = m[1] = -INFINITY;
       l[0] = l[1] = 0.f;
-      break;
     }
-    const uint32_t ks = smem_u32(smem + i * C::kStageBytes);
-    attend_tile<D>(qa, ks, ks + C::kTileBytes, 16, o, m, l, lane);
+  } else {
+    for (int i = 0; i < nb; ++i) {
+      if (!mbar_wait(&full[i], 0, 412)) {
+        // timed out (MG_ERR_TIMEOUT recorded): leave an empty state so the merge gives this slot no weight
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
+        break;
+      }
+      const uint32_t ks = smem_u32(smem + i * C::kStageBytes);
+      attend_tile<D>(qa, ks, ks + C::kTileBytes, 16, o, m, l, lane);
+    }
   }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -478,13 +608,13 @@ __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUt
   }
 }
 
-template <int D, bool T>
+template <int D, bool T, bool Q8>
 __global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(const __grid_constant__ CUtensorMap tk,
                                                               const __grid_constant__ CUtensorMap tv,
                                                               const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnCfg<D>::kBarOffset);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AttnCfg<D, Q8>::kBarOffset);
   uint64_t* empty = full + kStages;
   griddep_launch();
   if (threadIdx.x == 0) {
@@ -504,10 +634,10 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attn_kernel(const __grid_co
   if ((int)blockIdx.x < n_shared_ctas) {
     const int per_head = p.n_shared_ctas_per_head * p.n_row_groups;
     const int h = blockIdx.x / per_head, r = blockIdx.x % per_head;
-    shared_cta<D>(p, &tk, &tv, h, r / p.n_row_groups, r % p.n_row_groups, smem, full);
+    shared_cta<D, Q8>(p, &tk, &tv, h, r / p.n_row_groups, r % p.n_row_groups, smem, full);
   } else {
     const int i = blockIdx.x - n_shared_ctas;
-    private_cta<D, T>(p, &tk, &tv, i / p.nsplit, i % p.nsplit, smem, full, empty);
+    private_cta<D, T, Q8>(p, &tk, &tv, i / p.nsplit, i % p.nsplit, smem, full, empty);
   }
 }
 
@@ -569,26 +699,34 @@ Plan make_plan(int b, int hq, int hkv, int d, int max_blocks, int n_shared) {
   return pl;
 }
 
-template <int D>
+template <int D, bool Q8 = false>
 int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v_pool, cudaStream_t st) {
-  using C = AttnCfg<D>;
+  using C = AttnCfg<D, Q8>;
   static bool attr_done[64] = {};
   static std::mutex attr_mu;
   MG_CUDA_TRY(mg_once_per_device(attr_done, attr_mu, [] {
-    cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<D, true, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(paged_attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+      e = cudaFuncSetAttribute(paged_attn_kernel<D, false, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::kSmem);
     return e;
   }));
   // Pools as 2-D tensors [num_blocks*hkv*16 rows, D]: rows of one (block, kv head) tile are adjacent.
   const uint64_t rows = (uint64_t)p.num_blocks * p.hkv * 16;
   if (rows > 0x7fffffffull) return MG_ERR_UNSUPPORTED;
-  const CUtensorMapSwizzle sw = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUtensorMap tk, tv;
-  int rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
-  if (rc) return rc;
-  rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, v_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
+  int rc;
+  if constexpr (Q8) {  // int8 rows of d bytes, one box per tile, unswizzled (converted by the consumers)
+    rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_pool, D, rows, D, D, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_pool, D, rows, D, D, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    const CUtensorMapSwizzle sw = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
+    if (rc) return rc;
+    rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, v_pool, D, rows, D * 2, C::kBoxCols, 16, sw);
+  }
   if (rc) return rc;
   p.n_shared_ctas_per_head = pl.n_shared_ctas_per_head;
   p.n_row_groups = pl.n_row_groups;
@@ -596,10 +734,10 @@ int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v
                        (int64_t)p.b * p.hkv * pl.nsplit;
   if (ctas > 0x7fffffff) return MG_ERR_UNSUPPORTED;
   if (p.group <= 8) {
-    MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, true>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk, tv,
-                          p));
+    MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, true, Q8>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk,
+                          tv, p));
   } else {
-    MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, false>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk,
+    MG_CUDA_TRY(mg_launch(paged_attn_kernel<D, false, Q8>, dim3((unsigned)ctas), dim3(kThreads), C::kSmem, st, 1, tk,
                           tv, p));
   }
   if (!pl.direct) {
@@ -621,19 +759,22 @@ extern "C" int mg_paged_attn_workspace_bytes(int b, int hq, int hkv, int d, int 
   return MG_OK;
 }
 
-extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
-                                    const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,
-                                    int hq, int hkv, int d, int n_shared_blocks, float scale, void* out,
-                                    void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+
+int paged_attn(const float* q, const void* k_pool, const void* v_pool, const float* k_scales, const float* v_scales,
+               bool q8, int64_t num_blocks, const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens,
+               int b, int hq, int hkv, int d, int n_shared_blocks, float scale, void* out, void* workspace,
+               size_t workspace_bytes, void* stream) {
   if (b < 0 || hq <= 0 || hkv <= 0 || hq % hkv || hq / hkv > 16 || max_blocks <= 0 || num_blocks <= 0 ||
       n_shared_blocks < 0 || n_shared_blocks > max_blocks || !q || !k_pool || !v_pool || !block_tables ||
-      !ctx_lens || !out)
+      !ctx_lens || !out || (q8 && (!k_scales || !v_scales)))
     return MG_ERR_INVALID_ARG;
   if (d != 32 && d != 64 && d != 128) return MG_ERR_UNSUPPORTED;
   if (b == 0) return MG_OK;
   const Plan pl = make_plan(b, hq, hkv, d, max_blocks, n_shared_blocks);
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes)) return MG_ERR_INVALID_ARG;
-  if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) | reinterpret_cast<uintptr_t>(q)) & 15)
+  if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) | reinterpret_cast<uintptr_t>(q) |
+       reinterpret_cast<uintptr_t>(k_scales) | reinterpret_cast<uintptr_t>(v_scales)) & 15)
     return MG_ERR_INVALID_ARG;
   AttnParams p{};
   p.q = q;
@@ -655,9 +796,34 @@ extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const vo
   p.ws_o = static_cast<float*>(workspace);
   p.ws_ml = pl.ws_bytes ? static_cast<float*>(workspace) + (size_t)b * hq * pl.nslots * d : nullptr;
   p.direct = pl.direct;
+  p.k_scales = k_scales;
+  p.v_scales = v_scales;
   cudaStream_t st = mg_stream(stream);
+  if (q8) {
+    if (d == 32) return launch_attn<32, true>(p, pl, k_pool, v_pool, st);
+    return d == 64 ? launch_attn<64, true>(p, pl, k_pool, v_pool, st) : launch_attn<128, true>(p, pl, k_pool, v_pool, st);
+  }
   if (d == 32) return launch_attn<32>(p, pl, k_pool, v_pool, st);
   return d == 64 ? launch_attn<64>(p, pl, k_pool, v_pool, st) : launch_attn<128>(p, pl, k_pool, v_pool, st);
+}
+
+}  // namespace
+
+extern "C" int mg_paged_decode_attn(const float* q, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                    const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,
+                                    int hq, int hkv, int d, int n_shared_blocks, float scale, void* out,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  return paged_attn(q, k_pool, v_pool, nullptr, nullptr, false, num_blocks, block_tables, max_blocks, ctx_lens, b,
+                    hq, hkv, d, n_shared_blocks, scale, out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int mg_paged_decode_attn_kv8(const float* q, const int8_t* k_pool, const int8_t* v_pool,
+                                        const float* k_scales, const float* v_scales, int64_t num_blocks,
+                                        const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens, int b,
+                                        int hq, int hkv, int d, int n_shared_blocks, float scale, void* out,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  return paged_attn(q, k_pool, v_pool, k_scales, v_scales, true, num_blocks, block_tables, max_blocks, ctx_lens, b,
+                    hq, hkv, d, n_shared_blocks, scale, out, workspace, workspace_bytes, stream);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -266,14 +266,16 @@ class DecodeEngine:
     """Device state of one rank: weights, paged KV pool, step buffers, captured graphs."""
 
     def __init__(self, spec: ModelSpec, weights: ModelWeights, device, max_batch: int, num_blocks: int,
-                 max_blocks_per_seq: int, rank: int = 0, world: int = 1, group=None, max_pos: int = 0):
+                 max_blocks_per_seq: int, rank: int = 0, world: int = 1, group=None, max_pos: int = 0,
+                 quantize_kv: bool = False):
         self.spec, self.w, self.device = spec, weights, torch.device(device)
         self.rank, self.world, self.group = rank, world, group
         self.hq, self.hkv, self.D = spec.heads // world, spec.kv_heads // world, spec.head_dim
         self.inter = spec.inter // world
         self.max_batch, self.max_blocks = max_batch, max_blocks_per_seq
         self.max_ctx = max_blocks_per_seq * 16
-        self.pool = PagedKVPool(spec.layers, num_blocks, self.hkv, self.D, self.device)
+        # quantize_kv: int8 K/V codes with a per-vector scale (the reference's KVCacheState(quantize_kv=True))
+        self.pool = PagedKVPool(spec.layers, num_blocks, self.hkv, self.D, self.device, quantize=quantize_kv)
         self.scale = 1.0 / math.sqrt(self.D)
         dev = self.device
         if spec.family == "gpt2":
@@ -332,7 +334,7 @@ class DecodeEngine:
 
     def block_supported(self, world: int) -> bool:
         s, w = self.spec, self.w
-        if os.environ.get("MG_BLOCK", "0") != "1" or not isinstance(w.lm_q, K.PackedWeight):
+        if os.environ.get("MG_BLOCK", "0") != "1" or not isinstance(w.lm_q, K.PackedWeight) or self.pool.quantize:
             return False
         if self.max_batch > K.BLOCK_MAX_TOKENS or s.hidden % 128 or self.D not in (32, 64, 128):
             return False
@@ -444,7 +446,8 @@ class DecodeEngine:
         P = probe if probe is not None else (lambda kind, nbytes: contextlib.nullcontext())
         H, D = s.hidden, self.D
         nqkv = (self.hq + 2 * self.hkv) * D
-        attn_bytes = kv_tokens * self.hkv * D * 2 * 2 + b * self.hq * D * (4 + 2)
+        kv_vec = D + 4 if self.pool.quantize else 2 * D  # one K or V vector: bf16, or int8 codes + a scale
+        attn_bytes = kv_tokens * self.hkv * kv_vec * 2 + b * self.hq * D * (4 + 2)
         with P("embed", b * H * 8):
             K.embed(self.tokens[:b], self.positions[:b], w.embed, w.wpe, h)
         if self.block_args is not None:
@@ -455,7 +458,7 @@ class DecodeEngine:
                     with P("paged_attn", attn_bytes):
                         K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
                                             n_shared_blocks=n_shared_blocks, out=self.attn[:b],
-                                            workspace=self.workspace, validate=False)
+                                            workspace=self.workspace, validate=False, **self.pool.scales(l))
                 a.m = b
                 with P("decode_block", self.block_bytes(i, b)):
                     K.decode_block(a, self.block_ws, comm)
@@ -477,11 +480,12 @@ class DecodeEngine:
                             workspace=self.lin_ws)
             with P("rope_kv_append", b * nqkv * 4 + b * self.hq * D * 4 + b * 2 * self.hkv * D * 2):
                 K.rope_kv_append(self.qkv[:b], self.positions[:b], self.cos_sin, self.slots[:b], self.hq,
-                                 self.hkv, self.D, self.pool.k[l], self.pool.v[l], q_out=self.q[:b])
+                                 self.hkv, self.D, self.pool.k[l], self.pool.v[l], q_out=self.q[:b],
+                                 **self.pool.scales(l))
             with P("paged_attn", attn_bytes):
                 K.paged_decode_attn(self.q[:b], self.pool.k[l], self.pool.v[l], tab, ctx, self.scale,
                                     n_shared_blocks=n_shared_blocks, out=self.attn[:b], workspace=self.workspace,
-                                    validate=False)
+                                    validate=False, **self.pool.scales(l))
             if fused:
                 with P("i8_linear", self.linear_bytes(L.o_q, b, 0, H) + push_bytes):
                     K.i8_linear_rowpar(self.attn[:b], L.o_q, L.o_s, self.comm, workspace=self.lin_ws)
@@ -617,11 +621,12 @@ class DecodeEngine:
                 self._norm(h, Lw.ln1_w, Lw.ln1_b, x)
                 K.i8_linear(x, Lw.qkv_q, Lw.qkv_s, Lw.qkv_b, y=qkv, epilogue=K.EPI_STORE_F32)
                 K.rope_kv_append(qkv, posd, self.cos_sin, slots, self.hq, self.hkv, D, self.pool.k[l],
-                                 self.pool.v[l], q_out=q)
+                                 self.pool.v[l], q_out=q, **self.pool.scales(l))
                 for si in range(b):
                     r = slice(si * L, (si + 1) * L)
                     K.paged_decode_attn(q[r], self.pool.k[l], self.pool.v[l], tabd[r], ctx[r], self.scale,
-                                        n_shared_blocks=n_sh, out=attn[r], workspace=pf["ws"], validate=False)
+                                        n_shared_blocks=n_sh, out=attn[r], workspace=pf["ws"], validate=False,
+                                        **self.pool.scales(l))
                 bias_o = Lw.o_b if self.rank == 0 else None
                 row_parallel_residual(h, lambda y, e: K.i8_linear(attn, Lw.o_q, Lw.o_s, bias_o, y=y, epilogue=e),
                                       self.rank, self.world, self.group)

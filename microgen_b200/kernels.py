@@ -139,17 +139,28 @@ def i8_linear(x, q, scales, bias=None, y=None, epilogue=EPI_STORE_BF16, algo: st
     return y
 
 
-def rope_kv_append(qkv, positions, cos_sin, slots, hq, hkv, d, k_pool, v_pool, q_out=None):
+def rope_kv_append(qkv, positions, cos_sin, slots, hq, hkv, d, k_pool, v_pool, q_out=None, k_scales=None,
+                   v_scales=None):
+    """RoPE on q and k, K/V into their paged slots. int8 pools (with ``k_scales`` / ``v_scales`` fp32
+    [num_blocks, hkv, 16]) store each K and V vector quantized per vector (``mg_rope_kv_append_kv8``)."""
     _need(qkv, torch.float32, "qkv", contiguous=False)
     _need(slots, torch.int32, "slots")
-    _need(k_pool, torch.bfloat16, "k_pool")
-    _need(v_pool, torch.bfloat16, "v_pool")
     b = qkv.shape[0]
     if cos_sin is not None:
         _need(cos_sin, torch.float32, "cos_sin")
         _need(positions, torch.int32, "positions")
     if q_out is None:
         q_out = torch.empty((b, hq, d), dtype=torch.float32, device=qkv.device)
+    if k_pool.dtype == torch.int8:
+        _need(v_pool, torch.int8, "v_pool")
+        _need(k_scales, torch.float32, "k_scales")
+        _need(v_scales, torch.float32, "v_scales")
+        _lib.call("mg_rope_kv_append_kv8", _ptr(qkv), qkv.stride(0), _ptr(positions), _ptr(cos_sin),
+                  0 if cos_sin is None else cos_sin.shape[0], _ptr(slots), b, hq, hkv, d, _ptr(q_out), _ptr(k_pool),
+                  _ptr(v_pool), _ptr(k_scales), _ptr(v_scales), k_pool.shape[0], _stream())
+        return q_out
+    _need(k_pool, torch.bfloat16, "k_pool")
+    _need(v_pool, torch.bfloat16, "v_pool")
     _lib.call("mg_rope_kv_append", _ptr(qkv), qkv.stride(0), _ptr(positions), _ptr(cos_sin),
               0 if cos_sin is None else cos_sin.shape[0], _ptr(slots), b, hq, hkv, d, _ptr(q_out), _ptr(k_pool),
               _ptr(v_pool), k_pool.shape[0], _stream())
@@ -163,7 +174,7 @@ def attn_workspace_bytes(b, hq, hkv, d, max_blocks, n_shared_blocks=0) -> int:
 
 
 def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared_blocks=0, out=None,
-                      workspace=None, validate=True):
+                      workspace=None, validate=True, k_scales=None, v_scales=None):
     """q fp32 [b, hq, d]; pools bf16 [nblk, hkv, 16, d]; tables int32 [b, max_blocks]; ctx int32 [b].
     Returns bf16 [b, hq*d]. ``workspace`` (optional) is allocated when missing or too small.
 
@@ -173,8 +184,14 @@ def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared
     their host copy of the tables pass False). The kernel also records MG_ERR_DEVICE when it sees a
     mismatch."""
     _need(q, torch.float32, "q")
-    _need(k_pool, torch.bfloat16, "k_pool")
-    _need(v_pool, torch.bfloat16, "v_pool")
+    q8 = k_pool.dtype == torch.int8
+    if q8:  # INT8 KV: codes + one fp32 scale per (block, kv head, token) vector
+        _need(v_pool, torch.int8, "v_pool")
+        _need(k_scales, torch.float32, "k_scales")
+        _need(v_scales, torch.float32, "v_scales")
+    else:
+        _need(k_pool, torch.bfloat16, "k_pool")
+        _need(v_pool, torch.bfloat16, "v_pool")
     _need(block_tables, torch.int32, "block_tables")
     _need(ctx_lens, torch.int32, "ctx_lens")
     b, hq, d = q.shape
@@ -188,9 +205,14 @@ def paged_decode_attn(q, k_pool, v_pool, block_tables, ctx_lens, scale, n_shared
         workspace = torch.zeros(ws, dtype=torch.uint8, device=q.device)
     if out is None:
         out = torch.empty((b, hq * d), dtype=torch.bfloat16, device=q.device)
-    _lib.call("mg_paged_decode_attn", _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_tables),
-              max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks, float(scale), _ptr(out),
-              _ptr(workspace if ws else None), ws, _stream())
+    if q8:
+        _lib.call("mg_paged_decode_attn_kv8", _ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(k_scales), _ptr(v_scales),
+                  k_pool.shape[0], _ptr(block_tables), max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks,
+                  float(scale), _ptr(out), _ptr(workspace if ws else None), ws, _stream())
+    else:
+        _lib.call("mg_paged_decode_attn", _ptr(q), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
+                  _ptr(block_tables), max_blocks, _ptr(ctx_lens), b, hq, hkv, d, n_shared_blocks, float(scale),
+                  _ptr(out), _ptr(workspace if ws else None), ws, _stream())
     if ws:
         _lib.LAUNCHES[0] += 1  # the split-combine kernel
     return out

@@ -221,14 +221,32 @@ def block_table_tensor(tables: Sequence[BlockTable], max_blocks: int, device=Non
 
 
 class PagedKVPool:
-    """Per-layer K and V pools, bf16 ``[num_blocks, kv_heads, 16, head_dim]`` on one device."""
+    """Per-layer K and V pools ``[num_blocks, kv_heads, 16, head_dim]`` on one device: bf16, or with
+    ``quantize`` int8 codes plus one fp32 scale per (block, kv head, token) vector in ``k_scale`` /
+    ``v_scale`` ``[layers, num_blocks, kv_heads, 16]`` (the paged form of ``KVCacheState(quantize_kv=True)``,
+    ``kv_cache.py:30-40``)."""
 
     def __init__(self, layers: int, num_blocks: int, kv_heads: int, head_dim: int, device,
-                 dtype: torch.dtype = torch.bfloat16) -> None:
+                 dtype: torch.dtype = torch.bfloat16, quantize: bool = False) -> None:
         shape = (layers, num_blocks, kv_heads, BLOCK_SIZE, head_dim)
+        self.quantize = bool(quantize)
+        dtype = torch.int8 if self.quantize else dtype
         self.k = torch.zeros(shape, dtype=dtype, device=device)
         self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.k_scale = self.v_scale = None
+        if self.quantize:
+            self.k_scale = torch.zeros(shape[:4], dtype=torch.float32, device=device)
+            self.v_scale = torch.zeros(shape[:4], dtype=torch.float32, device=device)
         self.num_blocks = num_blocks
 
+    def scales(self, layer: int) -> dict:
+        """Keyword arguments naming layer ``layer``'s scale arrays for the KV kernels (none for bf16)."""
+        if not self.quantize:
+            return {}
+        return {"k_scales": self.k_scale[layer], "v_scales": self.v_scale[layer]}
+
     def nbytes(self) -> int:
-        return 2 * self.k.numel() * self.k.element_size()
+        n = 2 * self.k.numel() * self.k.element_size()
+        if self.quantize:
+            n += 2 * self.k_scale.numel() * 4
+        return n

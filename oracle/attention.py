@@ -56,3 +56,25 @@ def paged_decode_attention(q, k_pool, v_pool, block_tables, ctx_lens, scale: flo
         v = gather_contiguous(v_pool, block_tables[i], int(ctx_lens[i]))
         out[i] = sdpa_decode(q[i], k, v, scale)
     return out
+
+
+def quantize_kv_vectors(x):
+    """Per-vector INT8 of ``KVCacheState(quantize_kv=True)`` (``microgen/runtime/kv_cache.py:30-35``,
+    ``_quantize_tensor``): over the last axis, ``s = max(max|x| / 127, 1e-8)`` and
+    ``code = clamp(round_half_even(x / s), -128, 127)``, in float32 as the reference computes it.
+    Returns (int8 codes shaped like x, float32 scales with the last axis dropped)."""
+    x = np.asarray(x, dtype=np.float32)
+    s = np.maximum(np.abs(x).max(axis=-1, keepdims=True) / np.float32(127.0), np.float32(1e-8))
+    s = s.astype(np.float32)
+    q = np.clip(np.rint(x / s), -128, 127).astype(np.int8)
+    return q, s[..., 0]
+
+
+def paged_decode_attention_kv8(q, k_pool, v_pool, k_scale, v_scale, block_tables, ctx_lens,
+                               scale: float) -> np.ndarray:
+    """``paged_decode_attention`` over INT8 pools: K and V are the codes times their per-vector scales
+    (``_dequantize_tensor``, ``kv_cache.py:38-40``), evaluated in float64. Pools int8
+    ``[num_blocks, Hkv, BLOCK, D]``, scales ``[num_blocks, Hkv, BLOCK]``."""
+    k = k_pool.astype(np.float64) * k_scale.astype(np.float64)[..., None]
+    v = v_pool.astype(np.float64) * v_scale.astype(np.float64)[..., None]
+    return paged_decode_attention(q, k, v, block_tables, ctx_lens, scale)

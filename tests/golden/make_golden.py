@@ -27,6 +27,8 @@ Every array written here is an output of the reference's own code:
   ``prefill``/``decode`` on seeded tiny Llama / Qwen2 / GPT-2 models. For GPT-2
   the Conv1D projections are first rewrapped as ``nn.Linear`` (weight =
   ``Conv1D.weight.T``), because the reference quantizer only swaps ``nn.Linear``.
+* ``kv8_cases.npz`` (``--kv8``) — INT8 KV (``KVCacheState(quantize_kv=True)``): the per-vector
+  quantizer, SDPA over the stored INT8 cache, and a tiny-Llama greedy stream with that cache.
 * ``full_<shape>.npz`` (``--full``) — the same greedy stream at the full model
   shapes of the workloads (GPT-2-small, Qwen2.5-0.5B, Llama-3.2-3B; every layer,
   the full vocabulary) for a batch of two prompts: 64 greedy tokens per sequence,
@@ -300,6 +302,81 @@ def make_models(n_prompt=16, n_new=64, n_logits=8):
                             shape=json.dumps(shape))
 
 
+def make_kv8(n_prompt=16, n_new=32, n_logits=8):
+    """INT8 KV (``KVCacheState(quantize_kv=True)``, ``runtime/kv_cache.py:30-40, 114-120``): the reference's
+    per-vector quantizer on seeded and edge-case vectors; its stored codes and scales after two updates with
+    the SDPA decode output over their dequantization; and a tiny-Llama greedy stream decoded with an INT8
+    cache (``QuantizedPyTorchBackend``)."""
+    from microgen.runtime.kv_cache import _dequantize_tensor, _quantize_tensor
+    out = {}
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((64, 64), dtype=np.float32) * np.float32(3.0)
+    x[0] = 0.0                                        # the 1e-8 scale floor
+    x[1] = np.linspace(-1.0, 1.0, 64, dtype=np.float32)
+    x[2, :] = 0.5
+    x[2, 0] = 127.0                                   # exact .5 quotients: round half to even
+    x[3] = 1e-12                                      # tiny vector: floor scale, codes clamp at 127
+    q, sc = _quantize_tensor(torch.from_numpy(x))
+    out.update(quant_x=x, quant_q=q.numpy(), quant_s=sc.numpy()[:, 0])
+    # attention over the stored INT8 cache of the reference
+    B, Hq, Hkv, D, ctx = 2, 12, 4, 64, [37, 80]
+    L = max(ctx)
+    q_ = rng.standard_normal((B, Hq, D), dtype=np.float32)
+    k = rng.standard_normal((B, Hkv, L, D), dtype=np.float32)
+    v = rng.standard_normal((B, Hkv, L, D), dtype=np.float32)
+    alloc = PagedKVCacheAllocator(num_blocks=16 * B, block_size=16)
+    random.Random(22).shuffle(alloc._free_blocks)
+    maxb = (L + 15) // 16
+    tables = np.zeros((B, maxb), np.int32)
+    kpool = np.zeros((alloc.num_blocks, Hkv, 16, D), np.int8)
+    vpool = np.zeros_like(kpool)
+    kscale = np.zeros((alloc.num_blocks, Hkv, 16), np.float32)
+    vscale = np.zeros_like(kscale)
+    outs = np.zeros((B, Hq, D), np.float32)
+    for b in range(B):
+        cache = KVCacheState(max_seq_len=4096, quantize_kv=True)
+        kk = torch.from_numpy(k[b:b + 1, :, :ctx[b]])
+        vv = torch.from_numpy(v[b:b + 1, :, :ctx[b]])
+        split = ctx[b] // 2
+        cache.update(kk[:, :, :split], vv[:, :, :split], 0)
+        cache.update(kk[:, :, split:], vv[:, :, split:], 0)
+        kc, vc = cache.key_cache[0], cache.value_cache[0]          # int8 [1, Hkv, ctx, D]
+        ks, vs = cache.key_scales[0], cache.value_scales[0]        # fp32 [1, Hkv, ctx, 1]
+        bt = alloc.allocate_sequence(f"s{b}", ctx[b])
+        ids = [blk.block_id for blk in bt.physical_blocks]
+        tables[b, :len(ids)] = ids
+        for t in range(ctx[b]):
+            kpool[ids[t // 16], :, t % 16] = kc[0, :, t].numpy()
+            vpool[ids[t // 16], :, t % 16] = vc[0, :, t].numpy()
+            kscale[ids[t // 16], :, t % 16] = ks[0, :, t, 0].numpy()
+            vscale[ids[t // 16], :, t % 16] = vs[0, :, t, 0].numpy()
+        kd = _dequantize_tensor(kc, ks, torch.float32)
+        vd = _dequantize_tensor(vc, vs, torch.float32)
+        qq = torch.from_numpy(q_[b:b + 1, :, None, :])
+        o, _ = sdpa_attention_forward(_Attn(Hq // Hkv), qq, kd, vd, None, scaling=1.0 / np.sqrt(D))
+        outs[b] = o[0, 0].numpy()
+    out.update(attn_q=q_, attn_kpool=kpool, attn_vpool=vpool, attn_kscale=kscale, attn_vscale=vscale,
+               attn_tables=tables, attn_ctx=np.array(ctx, np.int32), attn_out=outs)
+    # tiny Llama greedy stream with an INT8 KV cache
+    shape = TINY["llama"]
+    model, _ = make_hf_model(shape, seed=0)
+    be = QuantizedPyTorchBackend(quant_type="int8")
+    be.load_model("tiny-llama", model_instance=model)
+    prompt = prompt_ids(shape["vocab"], n_prompt, seed=0)
+    logits, cache = be.prefill(torch.tensor([prompt], dtype=torch.long),
+                               cache=KVCacheState(max_seq_len=1024, quantize_kv=True))
+    toks, lg = [], []
+    for i in range(n_new):
+        tok = torch.argmax(logits, dim=-1, keepdim=True)
+        toks.append(int(tok.item()))
+        if i < n_logits:
+            lg.append(logits[0].numpy().copy())
+        logits, cache = be.decode(tok, cache=cache)
+    out.update(model_prompt=np.array(prompt, np.int64), model_tokens=np.array(toks, np.int64),
+               model_logits=np.stack(lg).astype(np.float32), model_shape=json.dumps(shape))
+    np.savez_compressed(os.path.join(HERE, "kv8_cases.npz"), **out)
+
+
 # Full-shape greedy streams: batch of two prompts of FULL_PROMPT ids; the Llama-3.2-3B shape shares
 # its first FULL_SHARED ids across the batch (the shared-prefix workload), the others share nothing.
 FULL_PROMPT, FULL_SHARED, FULL_NEW, FULL_LOGIT_STEPS, FULL_STRIDE, FULL_TOPK = 40, 32, 64, 4, 61, 16
@@ -356,6 +433,9 @@ def make_full_models(names=("GPT2_SMALL", "QWEN_05B", "LLAMA_3B")):
 
 
 if __name__ == "__main__":
+    if "--kv8" in sys.argv:
+        make_kv8()
+        sys.exit(0)
     if "--full" in sys.argv:
         make_full_models([a for a in sys.argv[1:] if a != "--full"] or ("GPT2_SMALL", "QWEN_05B", "LLAMA_3B"))
         sys.exit(0)

@@ -82,3 +82,22 @@ def test_model_oracle_greedy_matches_reference(family):
     assert toks == [int(t) for t in d["tokens"][:n]]
     for i in range(min(len(logits), d["logits"].shape[0])):
         np.testing.assert_allclose(logits[i], d["logits"][i], rtol=1e-3, atol=2e-4)
+
+
+def test_kv8_quantizer_oracle_bit_exact():
+    """The INT8-KV per-vector quantizer restated in the oracle equals the reference's ``_quantize_tensor``
+    (zero vectors on the 1e-8 floor, exact .5 quotients rounded half to even, tiny vectors clamped)."""
+    d = _npz("kv8_cases.npz")
+    q, s = oatt.quantize_kv_vectors(d["quant_x"])
+    assert np.array_equal(q, d["quant_q"])
+    assert np.array_equal(s.view(np.uint32), d["quant_s"].view(np.uint32))
+
+
+def test_kv8_attention_oracle_matches_reference():
+    """SDPA over the reference's stored INT8 cache (its codes and scales, dequantized) = the oracle over the
+    same codes and scales placed in paged pools."""
+    d = _npz("kv8_cases.npz")
+    D = d["attn_q"].shape[-1]
+    got = oatt.paged_decode_attention_kv8(d["attn_q"], d["attn_kpool"], d["attn_vpool"], d["attn_kscale"],
+                                          d["attn_vscale"], d["attn_tables"], d["attn_ctx"], 1.0 / np.sqrt(D))
+    np.testing.assert_allclose(got, d["attn_out"], rtol=1e-5, atol=1e-5)
