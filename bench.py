@@ -14,7 +14,11 @@ argmax). ``value`` = batch / device time per step (tokens/s), timed with CUDA ev
 CUDA-graph replays whose mean context equals the decode phase's mean (2048 + 256); the
 per-step working set (3.2 GB of weights + 4.8 GB of KV) is far larger than L2, so no flush
 is needed. ``e2e`` is the same decode through the backend's public API (host token ids in,
-greedy ids out) with the host<->device copies inside the timed region.
+greedy ids out) with the host<->device copies inside the timed region. At N > 1 the line also
+carries ``nvlink`` (the step's row-parallel push + reduce launches on their own) and
+``baseline_nccl``: the same step, weights, prompts and window with the row-parallel reduction as
+an NCCL all_reduce, timed the same way in the same run. ``--kv int8`` stores the KV cache as
+int8 codes with per-vector scales (the reference's ``quantize_kv``); the default is bf16.
 """
 
 from __future__ import annotations
@@ -48,6 +52,7 @@ def parse():
     ap.add_argument("--workload", default="llama3b", choices=sorted(WORKLOADS))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-nccl", action="store_true", help="N > 1: skip the same-run NCCL-reduce baseline")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (debug)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
     ap.add_argument("--sweep", default="", choices=["", "c4"],
@@ -726,6 +731,45 @@ def main():
                "d2h_bytes_per_step": B * 8, "ms_per_step": round(ems, 4)}
     K.check_device()
 
+    # ---- same-run NCCL baseline (N > 1): the same step with the row-parallel reduction as an NCCL
+    # all_reduce (store-or-add) instead of the fused peer push, device-timed the same way
+    nccl = None
+    if world > 1 and eng.comm is not None and not args.no_nccl:
+        log("nccl baseline")
+        os.environ["MG_FUSED_AR"] = "0"
+        be2 = B200TensorParallelBackend(world_size=world, group=group, **kw)
+        be2.load_state(spec, SyntheticState(spec, seed=0, device=torch.device("cuda", local)))
+        eng2 = be2.engine
+        lg2, cache2 = be2.prefill(prompts)
+        first2 = be2.sample(lg2)[:, 0].to(torch.int32).cpu()
+        for t in cache2.tables:
+            for _ in range(run + 1):
+                be2.allocator.append_token(t)
+        tab2 = block_table_tensor(cache2.tables, eng2.max_blocks)
+        eng2.set_inputs(first2.tolist(), [P] * B, [t.slot(P) for t in cache2.tables], [P + 1] * B, tab2)
+        g2 = eng2.capture(B, cache2.n_shared_blocks, advance=True)
+        for _ in range(skip + W):
+            g2.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record(stream)
+        for _ in range(Kst):
+            g2.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / Kst], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms2 = float(t.item())
+        nccl = {"value": round(B / (ms2 / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms2, 4),
+                "row_parallel_reduce": "nccl all_reduce (store-or-add), same weights / prompts / window",
+                "fused_over_nccl": round(ms2 / ms, 3),
+                "timing": f"CUDA graph of one step, {Kst} replays, CUDA events, max over ranks"}
+        del g2
+        eng2.release_graphs()
+        del be2, eng2, cache2, lg2
+        os.environ["MG_FUSED_AR"] = "1"
+
     cpu = None
     log("cpu baseline / report")
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -756,7 +800,7 @@ def main():
                   "timed_window_mean_ctx": round(mean_pos + 1)},
         "roofline": roofline, "step_roofline": step_roofline, "kernel_chains": chains, "nvlink": nvlink,
         "kernels": kernels,
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst,
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": per_step_launches * Kst, "baseline_nccl": nccl,
         "clocks": clk.summary(), "setup_s": {"load": round(t_load, 1), "prefill": round(t_prefill, 1)},
     }
     print(json.dumps(out), flush=True)

@@ -338,10 +338,18 @@ __device__ bool norm_row(const Params& p, const Ctx& cx, int row, const float* w
     uint64_t t0 = 0;
     for (int i = e; i < H / 2; i += kEpiThreads) {
       float a0 = __ldcg(hr + 2 * i), a1 = __ldcg(hr + 2 * i + 1);
-      for (int r = 0; r < po.world && ok; ++r) {
+      // every rank's word of this pair is loaded before any is used: one round trip for the world
+      uint64_t wds[MG_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < MG_MAX_RANKS; ++r)
+        if (r < po.world) wds[r] = *reinterpret_cast<const volatile uint64_t*>(base + (int64_t)r * po.slot + i);
+#pragma unroll
+      for (int r = 0; r < MG_MAX_RANKS && ok; ++r) {
+        if (r >= po.world) break;
         const uint64_t* wp = base + (int64_t)r * po.slot + i;
-        uint64_t wd;
+        uint64_t wd = wds[r];
         for (uint32_t spin = 0;; ++spin) {
+          if ((uint32_t)(wd >> 32) == epoch) break;
           wd = *reinterpret_cast<const volatile uint64_t*>(wp);
           if ((uint32_t)(wd >> 32) == epoch) break;
           if ((spin & 15) == 15) {

@@ -26,6 +26,8 @@
 // its own tile buffer, the shared CTA's warps together into a double buffer) and applies the scales
 // outside the MMAs: each score is multiplied by its key's scale, and each probability by its value's scale
 // before the PV product (the softmax sum uses the unscaled probabilities).
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace {
@@ -41,9 +43,12 @@ template <int D, bool Q8 = false>
 struct AttnCfg {
   static constexpr int kBf16Tile = 16 * D * 2;                // bf16 K (or V) of one block and kv head
   static constexpr int kTileBytes = Q8 ? 16 * D : kBf16Tile;  // as stored in the pool
-  static constexpr int kScaleOff = 2 * kTileBytes;            // Q8: 16 K scales, then 16 V scales
   static constexpr int kStageBytes = 2 * kTileBytes + (Q8 ? 128 : 0);
-  static constexpr int kRingBytes = kStages * kStageBytes;
+  // Q8 ring: kStages K tiles (TMA-swizzled so ldmatrix reads them without bank conflicts), then kStages V
+  // tiles, then kStages x 128 bytes of scales (16 K scales, 16 V scales per stage)
+  static constexpr int kVRing = kStages * kTileBytes;
+  static constexpr int kSRing = 2 * kStages * kTileBytes;
+  static constexpr int kRingBytes = Q8 ? kSRing + kStages * 128 : kStages * kStageBytes;
   static constexpr int kMergeBytes = kCons * 16 * (D + 2) * 4;
   static constexpr int kMain = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
   // Q8: converted bf16 tiles + their 32 scales, one buffer per consumer warp (the shared CTA uses two)
@@ -84,25 +89,46 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void mma_f16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Four int8 codes -> four exact f16 values: the biased byte b + 128 becomes the low mantissa bits of
+// 1024 (0x64 high byte), and 1152 is subtracted.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  const uint32_t a = __byte_perm(x, 0x64646464u, 0x4140), b = __byte_perm(x, 0x64646464u, 0x4342);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(0x64806480u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(0x64806480u));
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // TMA loads of the K and V tiles of (block phys, kv head h) into one ring stage; with Q8 the int8
-// tiles (one box of 16 rows x d bytes each) and the tiles' K and V scales (64 bytes each).
+// tiles (one box of 16 rows x d bytes each) and the tiles' K and V scales (64 bytes each). ring: the
+// CTA's ring base; s: the stage.
 template <int D, bool Q8 = false>
-__device__ __forceinline__ void load_stage(uint8_t* st, const CUtensorMap* tk, const CUtensorMap* tv, uint64_t* bar,
-                                           int row, const float* k_scales = nullptr,
+__device__ __forceinline__ void load_stage(uint8_t* ring, int s, const CUtensorMap* tk, const CUtensorMap* tv,
+                                           uint64_t* bar, int row, const float* k_scales = nullptr,
                                            const float* v_scales = nullptr) {
   using C = AttnCfg<D, Q8>;
   constexpr int T = C::kTileBytes;
   mbar_arrive_expect_tx(bar, C::kStageBytes);
   if constexpr (Q8) {
-    tma_load_2d(st, tk, bar, 0, row);
-    tma_load_2d(st + T, tv, bar, 0, row);
-    bulk_load_smem(st + C::kScaleOff, k_scales + row, 64, bar);
-    bulk_load_smem(st + C::kScaleOff + 64, v_scales + row, 64, bar);
+    tma_load_2d(ring + s * T, tk, bar, 0, row);
+    tma_load_2d(ring + C::kVRing + s * T, tv, bar, 0, row);
+    bulk_load_smem(ring + C::kSRing + s * 128, k_scales + row, 64, bar);
+    bulk_load_smem(ring + C::kSRing + s * 128 + 64, v_scales + row, 64, bar);
   } else {
+    uint8_t* st = ring + s * C::kStageBytes;
 #pragma unroll
     for (int c = 0; c < D; c += C::kBoxCols) {
       tma_load_2d(st + c * 32, tk, bar, c, row);  // 16 rows x 128 B = 2 KB per 64 columns
@@ -111,18 +137,30 @@ __device__ __forceinline__ void load_stage(uint8_t* st, const CUtensorMap* tk, c
   }
 }
 
-// Q8: the int8 K and V tiles of a stage -> exact bf16 integers in the swizzled tile layout of the bf16
-// path at dst (K, then V), and the stage's scales after them (V scales of tokens >= valid become 0, so a
-// zero probability never meets a stale scale). Threads t, t + n, ... of the n taking part.
+// Q8: byte offset of (row, byte) in a stage's int8 K tile, as TMA wrote it: 16 rows of d bytes with the
+// 16-byte chunks XOR-swizzled (128/64/32-byte swizzle for d = 128/64/32: offset bits 4.. ^= bits 7..).
 template <int D>
-__device__ __forceinline__ void convert_stage(const uint8_t* st, uint8_t* dst, int valid, int t, int n) {
+__device__ __forceinline__ uint32_t k8_off(int row, int byte) {
+  constexpr uint32_t kMask = D == 128 ? 7u : (D == 64 ? 3u : 1u);
+  const uint32_t o = (uint32_t)(row * D + byte);
+  return o ^ (((o >> 7) & kMask) << 4);
+}
+
+// Q8: a stage's int8 tiles -> exact bf16 integers in the swizzled tile layout of the bf16 path at dst (K
+// when with_k, then V at dst + one bf16 tile), and the stage's scales after them (V scales of tokens >=
+// valid become 0, so a zero probability never meets a stale scale). Threads t, t + n, ... take part.
+template <int D>
+__device__ __forceinline__ void convert_stage(const uint8_t* ring, int s, uint8_t* dst, int valid, int t, int n,
+                                              bool with_k) {
   using C = AttnCfg<D, true>;
   constexpr int kChunks = 16 * D / 16;  // 16-byte chunks per int8 tile
   const uint32_t dk = smem_u32(dst);
-  for (int c = t; c < 2 * kChunks; c += n) {
+  const uint8_t* kt = ring + s * C::kTileBytes;
+  const uint8_t* vt = ring + C::kVRing + s * C::kTileBytes;
+  for (int c = with_k ? t : kChunks + t; c < 2 * kChunks; c += n) {
     const int kv = c >= kChunks, cc = c - kv * kChunks;
     const int row = cc / (D / 16), col = (cc % (D / 16)) * 16;
-    const uint4 w = *reinterpret_cast<const uint4*>(st + kv * C::kTileBytes + cc * 16);
+    const uint4 w = *reinterpret_cast<const uint4*>(kv ? vt + cc * 16 : kt + k8_off<D>(row, col));
     uint32_t r[8];
     i8x4_to_bf16x4(w.x, r[0], r[1]);
     i8x4_to_bf16x4(w.y, r[2], r[3]);
@@ -137,7 +175,7 @@ __device__ __forceinline__ void convert_stage(const uint8_t* st, uint8_t* dst, i
                  : "memory");
   }
   for (int j = t; j < 32; j += n) {
-    const float v = reinterpret_cast<const float*>(st + C::kScaleOff)[j];
+    const float v = reinterpret_cast<const float*>(ring + C::kSRing + s * 128)[j];
     reinterpret_cast<float*>(dst + 2 * C::kBf16Tile)[j] = (j >= 16 && j - 16 >= valid) ? 0.f : v;
   }
 }
@@ -239,11 +277,8 @@ __device__ __forceinline__ void attend_tile(const uint32_t (&qa)[D / 16][4], uin
 // qb: B fragments of Qᵀ (k = dims, n = heads); o: Oᵀ accumulators (rows = dims, cols = heads);
 // m, l: running max / sum of heads 2t and 2t+1 (t = lane % 4).
 template <int D>
-__device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], uint32_t ks, uint32_t vs, int valid,
-                                              float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane,
-                                              const float* sc = nullptr) {
-  const int g = lane >> 2, t = lane & 3;
-  float s[4] = {0.f, 0.f, 0.f, 0.f};
+__device__ __forceinline__ void scores_t(const uint32_t (&qb)[D / 16][2], uint32_t ks, float (&s)[4], int lane) {
+  s[0] = s[1] = s[2] = s[3] = 0.f;
   const int arow = lane & 15, acol = (lane >> 4) * 8;
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
@@ -251,6 +286,35 @@ __device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], u
     ldsm_x4(ks + swz<D>(arow, kk * 16 + acol), a[0], a[1], a[2], a[3]);
     mma_bf16(s, a, qb[kk][0], qb[kk][1]);
   }
+}
+
+// Q8 form of scores_t: K straight from the stage's int8 tile (kt). ldmatrix hands lane (g, t) four
+// consecutive codes of rows g and g + 8 per 16-byte slice; converted to f16 they fill the MMA's k slots
+// 2t, 2t+1, 2t+8, 2t+9 with dims 4t .. 4t+3 of each 16-dim slice, and the query fragments (load_qt8) are
+// laid out in the same order, so the dot products are unchanged.
+template <int D>
+__device__ __forceinline__ void scores_t8(const uint32_t (&qb)[D / 16][2], uint32_t kt, float (&s)[4], int lane) {
+  s[0] = s[1] = s[2] = s[3] = 0.f;
+  const int row = (lane & 7) + ((lane >> 3) & 1) * 8, half = lane >> 4;
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    uint32_t r0, r1, r2, r3;
+    ldsm_x4(kt + k8_off<D>(row, 32 * j + 16 * half), r0, r1, r2, r3);
+    uint32_t a[4], b[4];
+    i8x4_to_f16x4(r0, a[0], a[2]);
+    i8x4_to_f16x4(r1, a[1], a[3]);
+    mma_f16(s, a, qb[2 * j][0], qb[2 * j][1]);
+    i8x4_to_f16x4(r2, b[0], b[2]);
+    i8x4_to_f16x4(r3, b[1], b[3]);
+    mma_f16(s, b, qb[2 * j + 1][0], qb[2 * j + 1][1]);
+  }
+}
+
+// Online softmax and Oᵀ += Vᵀ Pᵀ for a tile whose scores Sᵀ (scores_t / scores_t8) are in s.
+template <int D>
+__device__ __forceinline__ void softmax_pv_t(float (&s)[4], uint32_t vs, int valid, float (&o)[D / 16][4],
+                                             float (&m)[2], float (&l)[2], int lane, const float* sc) {
+  const int g = lane >> 2, t = lane & 3;
   if (sc) {  // Q8: key scales (rows g and g + 8 are keys)
     const float k0 = sc[g], k1 = sc[g + 8];
     s[0] *= k0;
@@ -303,6 +367,31 @@ __device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], u
     uint32_t a[4];
     ldsm_x4_t(vs + swz<D>(vtok, dt * 16 + vdim), a[0], a[1], a[2], a[3]);
     mma_bf16(o[dt], a, b0, b1);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], uint32_t ks, uint32_t vs, int valid,
+                                              float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane,
+                                              const float* sc = nullptr) {
+  float s[4];
+  scores_t<D>(qb, ks, s, lane);
+  softmax_pv_t<D>(s, vs, valid, o, m, l, lane, sc);
+}
+
+// Q8 query fragments for scores_t8 (f16): slot pairs (2t, 2t+1) and (2t+8, 2t+9) of each 16-dim slice
+// hold dims 4t, 4t+1 and 4t+2, 4t+3 of it.
+template <int D>
+__device__ __forceinline__ void load_qt8(uint32_t (&qb)[D / 16][2], const float* qh0, int group, float qscale,
+                                         int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const float* qh = g < group ? qh0 + g * D : nullptr;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int base = (kk >> 1) * 32 + (kk & 1) * 16 + 4 * t;
+    const float4 v = qh ? *reinterpret_cast<const float4*>(qh + base) : make_float4(0.f, 0.f, 0.f, 0.f);
+    qb[kk][0] = pack_f16x2(v.x * qscale, v.y * qscale);
+    qb[kk][1] = pack_f16x2(v.z * qscale, v.w * qscale);
   }
 }
 
@@ -411,14 +500,15 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
         const int s = i % kStages;
         if (i >= kStages) ok = mbar_wait(&empty[s], ((i / kStages) - 1) & 1, 411);
         if (ok)
-          load_stage<D, Q8>(smem + s * C::kStageBytes, tk, tv, &full[s], (int)((phys * p.hkv + h) * 16), p.k_scales,
-                            p.v_scales);
+          load_stage<D, Q8>(smem, s, tk, tv, &full[s], (int)((phys * p.hkv + h) * 16), p.k_scales, p.v_scales);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
   } else {
     uint32_t qa[D / 16][T ? 2 : 4];
-    if constexpr (T) {
+    if constexpr (T && Q8) {
+      load_qt8<D>(qa, p.q + ((int64_t)seq * p.hq + h * p.group) * D, p.group, p.qscale, lane);
+    } else if constexpr (T) {
       load_qt<D>(qa, p.q + ((int64_t)seq * p.hq + h * p.group) * D, p.group, p.qscale, lane);
     } else {
       load_q<D>(qa, p.q, p.hq, g0 < p.group ? seq : -1, h * p.group + g0, g1 < p.group ? seq : -1,
@@ -428,19 +518,27 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
       const int s = i % kStages;
       if (!mbar_wait(&full[s], (i / kStages) & 1, 410)) break;
       const int valid = min(16, ctx - (b0 + i) * 16);
-      if constexpr (Q8) {
-        // the stage's codes become this warp's bf16 tile; the stage is released once they are stored
+      if constexpr (Q8 && T) {
+        // V codes become this warp's bf16 tile and the scales are copied beside it; K is read from the stage
+        // itself, which is released once the score MMAs have consumed it
         uint8_t* wb = smem + C::kBufOffset + warp * C::kBufBytes;
-        convert_stage<D>(smem + s * C::kStageBytes, wb, valid, lane, 32);
+        convert_stage<D>(smem, s, wb, valid, lane, 32, false);
+        __syncwarp();
+        float sct[4];
+        scores_t8<D>(qa, smem_u32(smem + s * C::kTileBytes), sct, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        softmax_pv_t<D>(sct, smem_u32(wb) + C::kBf16Tile, valid, o, m, l, lane,
+                        reinterpret_cast<const float*>(wb + 2 * C::kBf16Tile));
+        __syncwarp();  // every lane is done with the buffer before the next conversion
+      } else if constexpr (Q8) {
+        // the stage's codes become this warp's bf16 tiles; the stage is released once they are stored
+        uint8_t* wb = smem + C::kBufOffset + warp * C::kBufBytes;
+        convert_stage<D>(smem, s, wb, valid, lane, 32, true);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         const uint32_t ks = smem_u32(wb), vs = ks + C::kBf16Tile;
-        const float* sc = reinterpret_cast<const float*>(wb + 2 * C::kBf16Tile);
-        if constexpr (T) {
-          attend_tile_t<D>(qa, ks, vs, valid, o, m, l, lane, sc);
-        } else {
-          attend_tile<D>(qa, ks, vs, valid, o, m, l, lane, sc);
-        }
+        attend_tile<D>(qa, ks, vs, valid, o, m, l, lane, reinterpret_cast<const float*>(wb + 2 * C::kBf16Tile));
         __syncwarp();  // every lane is done with the buffer before the next conversion
       } else {
         const uint32_t ks = smem_u32(smem + s * C::kStageBytes), vs = ks + C::kTileBytes;
@@ -536,8 +634,7 @@ __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUt
     for (int i = 0; i < nb; ++i) {
       const int64_t ph = __shfl_sync(0xffffffffu, phys, i);
       if (lane == 0)
-        load_stage<D, Q8>(smem + i * C::kStageBytes, tk, tv, &full[i], (int)((ph * p.hkv + h) * 16), p.k_scales,
-                          p.v_scales);
+        load_stage<D, Q8>(smem, i, tk, tv, &full[i], (int)((ph * p.hkv + h) * 16), p.k_scales, p.v_scales);
     }
     return;
   }
@@ -564,7 +661,7 @@ __device__ void shared_cta(const AttnParams& p, const CUtensorMap* tk, const CUt
       const bool ok = mbar_wait(&full[i], 0, 412);
       bad |= !ok;
       uint8_t* buf = smem + C::kBufOffset + (i & 1) * C::kBufBytes;
-      if (ok) convert_stage<D>(smem + i * C::kStageBytes, buf, 16, threadIdx.x, kCons * 32);
+      if (ok) convert_stage<D>(smem, i, buf, 16, threadIdx.x, kCons * 32, true);
       asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
       if (!bad && t * 16 < rows) {
         const uint32_t ks = smem_u32(buf);
@@ -649,13 +746,36 @@ __global__ void combine_kernel(const float* __restrict__ ws_o, const float* __re
   const int64_t sh = blockIdx.x;  // seq * hq + head
   const int d = threadIdx.x;
   const float* ml = ws_ml + sh * nslots * 2;
+  const float* wo = ws_o + sh * nslots * D + d;
+  // Slots are read eight at a time with every load of a group issued before any is used, so a merge of
+  // n slots waits on about n / 4 memory round trips rather than 2n; the sums keep slot order.
+  constexpr int kG = 8;
   float M = -INFINITY;
-  for (int s = 0; s < nslots; ++s) M = fmaxf(M, ml[2 * s]);
+  for (int s0 = 0; s0 < nslots; s0 += kG) {
+    float mv[kG];
+#pragma unroll
+    for (int j = 0; j < kG; ++j) mv[j] = s0 + j < nslots ? ml[2 * (s0 + j)] : -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kG; ++j) M = fmaxf(M, mv[j]);
+  }
   float L = 0.f, O = 0.f;
-  for (int s = 0; s < nslots; ++s) {
-    const float w = M == -INFINITY ? 0.f : exp2f(ml[2 * s] - M);
-    L += ml[2 * s + 1] * w;
-    O += ws_o[(sh * nslots + s) * D + d] * w;
+  for (int s0 = 0; s0 < nslots; s0 += kG) {
+    float mv[kG], lv[kG], ov[kG];
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+      const bool in = s0 + j < nslots;
+      mv[j] = in ? ml[2 * (s0 + j)] : -INFINITY;
+      lv[j] = in ? ml[2 * (s0 + j) + 1] : 0.f;
+      ov[j] = in ? wo[(int64_t)(s0 + j) * D] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+      if (s0 + j < nslots) {
+        const float w = M == -INFINITY ? 0.f : exp2f(mv[j] - M);
+        L += lv[j] * w;
+        O += ov[j] * w;
+      }
+    }
   }
   out[sh * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
 }
@@ -717,8 +837,10 @@ int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v
   if (rows > 0x7fffffffull) return MG_ERR_UNSUPPORTED;
   CUtensorMap tk, tv;
   int rc;
-  if constexpr (Q8) {  // int8 rows of d bytes, one box per tile, unswizzled (converted by the consumers)
-    rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_pool, D, rows, D, D, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if constexpr (Q8) {  // int8 rows of d bytes, one box per tile; K swizzled for the consumers' ldmatrix reads
+    const CUtensorMapSwizzle ksw = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                            : (D == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_pool, D, rows, D, D, 16, ksw);
     if (rc) return rc;
     rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_pool, D, rows, D, D, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
   } else {

@@ -393,7 +393,7 @@ def decode_block(args: BlockArgs, workspace: torch.Tensor, comm=None) -> None:
     """One launch of the persistent decode layer described by ``args`` (see ``mg_decode_block``).
     ``workspace``: a zero-filled uint8 device tensor of at least ``block_workspace_bytes(args)`` bytes,
     reused across launches; ``comm``: the row-parallel communicator at world > 1."""
-    _lib.call("mg_decode_block", C.byref(args), C.c_void_p(comm.handle if comm is not None else 0),
+    _lib.call("mg_decode_block", C.byref(args), comm.handle if comm is not None else None,
               _ptr(workspace), workspace.numel(), _stream())
 
 

@@ -52,9 +52,10 @@ def _prompts(shape=SHAPE):
     return [shared + prompt_ids(shape["vocab"], 9, seed=20 + i) for i in range(4)]
 
 
-def _worker(rank, world, port, outdir, graph, forced, fused, shape=SHAPE):
+def _worker(rank, world, port, outdir, graph, forced, fused, shape=SHAPE, block=False):
     import torch.distributed as dist
     os.environ["MG_FUSED_AR"] = "1" if fused else "0"
+    os.environ["MG_BLOCK"] = "1" if block else "0"
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from microgen_b200.backends import B200TensorParallelBackend
     from tests._hf_models import make_hf_model
@@ -67,6 +68,7 @@ def _worker(rank, world, port, outdir, graph, forced, fused, shape=SHAPE):
     be.load_model("tiny", model_instance=model)
     out = _decode(be, _prompts(shape), forced)
     assert (be.engine.comm is not None) == fused
+    assert (be.engine.block_args is not None) == block
     assert be.engine.vocab_parallel and be.engine.vocab_local < shape["vocab"]
     be.engine.release_graphs()
     torch.save(out, os.path.join(outdir, f"r{rank}.pt"))
@@ -82,14 +84,17 @@ ODD_VOCAB = dict(SHAPE, vocab=1001)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("fused,graph,shape", [(True, False, SHAPE), (True, True, SHAPE), (False, False, SHAPE),
-                                               (False, True, SHAPE), (True, True, ODD_VOCAB),
-                                               (False, True, ODD_VOCAB)],
-                         ids=["fused_push-eager", "fused_push-graph", "nccl-eager", "nccl-graph",
-                              "fused_push-graph-vocab1001", "nccl-graph-vocab1001"])
-def test_tp2_matches_tp1(graph, fused, shape):
+@pytest.mark.parametrize("fused,graph,shape,block", [
+    (True, False, SHAPE, False), (True, True, SHAPE, False), (False, False, SHAPE, False),
+    (False, True, SHAPE, False), (True, True, ODD_VOCAB, False), (False, True, ODD_VOCAB, False),
+    (True, True, SHAPE, True)],
+    ids=["fused_push-eager", "fused_push-graph", "nccl-eager", "nccl-graph", "fused_push-graph-vocab1001",
+         "nccl-graph-vocab1001", "persistent-layer-graph"])
+def test_tp2_matches_tp1(graph, fused, shape, block):
     """TP=2 with a vocab-parallel lm_head (each rank streams half of it; the greedy token is merged
-    across ranks on the device) against TP=1."""
+    across ranks on the device) against TP=1; the last case runs every layer's linears, norms and
+    RoPE / K/V append through the persistent layer kernel, whose row-parallel outputs go to the peers
+    from its epilogue and are reduced inside the same launch."""
     import torch.multiprocessing as mp
     from microgen_b200.backends import B200QuantizedBackend
     from tests._hf_models import make_hf_model
@@ -98,7 +103,7 @@ def test_tp2_matches_tp1(graph, fused, shape):
     be.load_model("tiny", model_instance=model)
     ref_toks, ref_lg, _ = _decode(be, _prompts(shape))
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks, fused, shape), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _port(), d, graph, ref_toks, fused, shape, block), nprocs=2, join=True)
         outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(2)]
     tol = 1e-2 + 2e-2 * np.abs(ref_lg)
     top2 = np.sort(ref_lg, axis=-1)[..., -2:]
