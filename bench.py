@@ -55,8 +55,9 @@ def parse():
     ap.add_argument("--no-nccl", action="store_true", help="N > 1: skip the same-run NCCL-reduce baseline")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (debug)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures)")
-    ap.add_argument("--sweep", default="", choices=["", "c4"],
-                    help="c4: the isolated INT8-linear and paged-attention kernel sweep, one JSON line per case")
+    ap.add_argument("--sweep", default="", choices=["", "c4", "scheduler"],
+                    help="c4: the isolated INT8-linear and paged-attention kernel sweep, one JSON line per case; "
+                         "scheduler: continuous batching throughput, batched decode vs one decode per request")
     ap.add_argument("--kv", default="bf16", choices=["bf16", "int8"],
                     help="KV cache storage: bf16 (the workload's default) or int8 codes with per-vector scales "
                          "(the reference's quantize_kv option)")
@@ -220,6 +221,89 @@ def _timed(fn, reps: int, flush) -> float:
         b.record(st)
     torch.cuda.synchronize()
     return 1e3 * sum(a.elapsed_time(b) for a, b in evs) / reps
+
+
+def sweep_scheduler(args) -> None:
+    """Continuous batching on one GPU, the workload's model shape: 48 requests with prompts of 192-320 ids
+    (a 128-id prefix shared by half of them), 48 new tokens each, greedy, at most 32 running. Two runs over
+    the same requests and backend: ``BatchedScheduler`` (one decode step for all running requests) and the
+    reference scheduler's decode loop (``scheduler.py:199-226``: one ``decode`` + ``sample`` per running
+    request and step, batch 1), both with the same admission and prefill. Wall-clock tokens/s of generated
+    tokens, prefill included; one JSON line per run."""
+    import torch
+    from microgen_b200 import model_spec as MS
+    from microgen_b200.backends import B200QuantizedBackend
+    from microgen_b200.scheduler import BatchedScheduler, Request, RequestStatus
+    from microgen_b200.synthetic import SyntheticState
+    torch.cuda.set_device(0)
+    wl = dict(WORKLOADS[args.workload])
+    shape = dict(getattr(MS, wl["shape"]))
+    if args.layers:
+        shape["layers"] = args.layers
+    spec = MS.ModelSpec(**shape)
+    n_req, new, max_run = 48, 48, 32
+    be = B200QuantizedBackend(max_batch=max_run, max_seq_len=512, num_blocks=max_run * 24 + 64, free_list_seed=0,
+                              prefix_cache_capacity=8)
+    be.load_state(spec, SyntheticState(spec, seed=0, device=torch.device("cuda", 0)))
+    g = torch.Generator().manual_seed(3)
+    shared = torch.randint(0, spec.vocab, (128,), generator=g).tolist()
+
+    def requests():
+        out = []
+        for i in range(n_req):
+            n = 192 + (i * 37) % 129
+            ids = torch.randint(0, spec.vocab, (n,), generator=g).tolist()
+            if i % 2 == 0:
+                ids[:128] = shared
+            out.append(Request(request_id=f"r{i}", prompt="", prompt_ids=ids, max_new_tokens=new, temperature=0.0))
+        return out
+
+    class Batched(BatchedScheduler):
+        decode_s = 0.0
+
+        def _decode(self, reqs):
+            t0 = time.perf_counter()
+            done = super()._decode(reqs)
+            self.decode_s += time.perf_counter() - t0  # the sampled ids reached the host inside
+            return done
+
+    class PerRequest(Batched):
+        """The reference scheduler's decode loop: every running request decoded on its own (batch 1)."""
+
+        def _decode(self, reqs):
+            t0 = time.perf_counter()
+            done = []
+            for r in list(reqs):
+                self._batch.tables = [self._tables[r.request_id]]
+                self._batch.n_shared_blocks = 0
+                self._batch.mirror = None
+                lg, _ = self.backend.decode(torch.tensor([[r.generated_token_ids[-1]]]), cache=self._batch)
+                done += self._finish([r], self._sample_rows([r], lg))
+            self.decode_batch_sizes.append(1)
+            self.decode_s += time.perf_counter() - t0
+            return done
+
+    for name, cls in (("batched", Batched), ("per_request", PerRequest), ("batched", Batched)):
+        reqs = requests()
+        sch = cls(be, max_batch_size=max_run)
+        for r in reqs:
+            sch.add_request(r)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        sch.run_until_complete()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        assert all(r.status == RequestStatus.COMPLETED for r in reqs)
+        toks = sum(len(r.generated_token_ids) for r in reqs)
+        print(json.dumps({"sweep": "scheduler", "scheduler": name, "workload": f"{args.workload} shape "
+                          f"({spec.layers} layers), {n_req} requests, prompts 192-320 (128 shared by half), "
+                          f"{new} new tokens each, <= {max_run} running", "generated_tokens": toks,
+                          "seconds": round(dt, 3), "tokens_per_s": round(toks / dt, 1),
+                          "decode_seconds": round(sch.decode_s, 3),
+                          "decode_tokens_per_s": round((toks - n_req) / sch.decode_s, 1),
+                          "decode_steps": len(sch.decode_batch_sizes),
+                          "mean_decode_batch": round(sum(sch.decode_batch_sizes) / max(1, len(sch.decode_batch_sizes)), 2),
+                          "profile_ms": {k: round(v, 1) for k, v in sch.get_profile_breakdown().items()}}), flush=True)
 
 
 def sweep_c4(args) -> None:
@@ -519,6 +603,9 @@ def main():
         return
     if args.sweep == "c4":
         sweep_c4(args)
+        return
+    if args.sweep == "scheduler":
+        sweep_scheduler(args)
         return
     import torch
     import torch.distributed as dist
