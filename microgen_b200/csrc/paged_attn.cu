@@ -21,11 +21,13 @@
 // writes the normalised output itself.
 //
 // INT8 KV (Q8): pools are int8 [num_blocks, hkv, 16, d] with one fp32 scale per (block, kv head,
-// token) vector for K and for V. A stage holds the int8 K and V tiles (TMA, no swizzle) and their 16 + 16
-// scales (bulk copies). The consumer converts the integer codes exactly to bf16 (a private CTA's warp into
-// its own tile buffer, the shared CTA's warps together into a double buffer) and applies the scales
-// outside the MMAs: each score is multiplied by its key's scale, and each probability by its value's scale
-// before the PV product (the softmax sum uses the unscaled probabilities).
+// token) vector for K and for V. A stage holds the int8 K and V tiles (TMA, swizzled) and their 16 + 16
+// scales (bulk copies). Private CTAs of the transposed form feed the codes from the stage straight into f16
+// MMA fragments (exact integer conversion in registers; K and V fragment orders chosen so ldmatrix can
+// deliver them); the other forms convert the codes exactly to bf16 first (a warp into its own tile buffer,
+// the shared CTA's warps together into a double buffer). Scales apply outside the MMAs: each score is
+// multiplied by its key's scale, and each probability by its value's scale before the PV product (the
+// softmax sum uses the unscaled probabilities).
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -44,8 +46,8 @@ struct AttnCfg {
   static constexpr int kBf16Tile = 16 * D * 2;                // bf16 K (or V) of one block and kv head
   static constexpr int kTileBytes = Q8 ? 16 * D : kBf16Tile;  // as stored in the pool
   static constexpr int kStageBytes = 2 * kTileBytes + (Q8 ? 128 : 0);
-  // Q8 ring: kStages K tiles (TMA-swizzled so ldmatrix reads them without bank conflicts), then kStages V
-  // tiles, then kStages x 128 bytes of scales (16 K scales, 16 V scales per stage)
+  // Q8 ring: kStages K tiles, then kStages V tiles (TMA-swizzled so ldmatrix reads them without bank
+  // conflicts), then kStages x 128 bytes of scales (16 K scales, 16 V scales per stage)
   static constexpr int kVRing = kStages * kTileBytes;
   static constexpr int kSRing = 2 * kStages * kTileBytes;
   static constexpr int kRingBytes = Q8 ? kSRing + kStages * 128 : kStages * kStageBytes;
@@ -108,6 +110,14 @@ __device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(0x64806480u));
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(0x64806480u));
 }
+// The four codes of a 16-bit-pair register (bytes: token a dim c, token a dim c+1, token b dim c, token b
+// dim c+1) -> f16 pairs (dim c: tokens a, b) and (dim c+1: tokens a, b), exactly.
+__device__ __forceinline__ void i8pairs_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  const uint32_t a = __byte_perm(x, 0x64646464u, 0x4240), b = __byte_perm(x, 0x64646464u, 0x4341);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(0x64806480u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(0x64806480u));
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -160,7 +170,7 @@ __device__ __forceinline__ void convert_stage(const uint8_t* ring, int s, uint8_
   for (int c = with_k ? t : kChunks + t; c < 2 * kChunks; c += n) {
     const int kv = c >= kChunks, cc = c - kv * kChunks;
     const int row = cc / (D / 16), col = (cc % (D / 16)) * 16;
-    const uint4 w = *reinterpret_cast<const uint4*>(kv ? vt + cc * 16 : kt + k8_off<D>(row, col));
+    const uint4 w = *reinterpret_cast<const uint4*>((kv ? vt : kt) + k8_off<D>(row, col));
     uint32_t r[8];
     i8x4_to_bf16x4(w.x, r[0], r[1]);
     i8x4_to_bf16x4(w.y, r[2], r[3]);
@@ -370,6 +380,76 @@ __device__ __forceinline__ void softmax_pv_t(float (&s)[4], uint32_t vs, int val
   }
 }
 
+// Q8: probabilities enter the PV MMA in f16, times the value scale and this power of two so that small
+// ones stay normal; l carries the same factor, removed before a CTA's partial state leaves it.
+constexpr float kPScale = 256.f;
+
+// Q8 form of softmax_pv_t: V straight from the stage's int8 tile (vt, swizzled like K; sc: the stage's 16 K
+// then 16 V scales). ldmatrix.trans of the codes as 16-bit pairs hands lane (g, t) the codes of tokens 2t and
+// 2t + 1 at dims 2g and 2g + 1 of a 16-dim slice (and tokens 2t + 8, 2t + 9 from the second matrix); split by
+// byte they are exactly the A fragment of Vᵀ with MMA row g holding dim 2g and row g + 8 dim 2g + 1 — the
+// Oᵀ accumulators keep that order. Value scales of slots past `valid` are taken as 0.
+template <int D>
+__device__ __forceinline__ void softmax_pv_t8(float (&s)[4], uint32_t vt, const float* sc, int valid,
+                                              float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  {
+    const float k0 = sc[g], k1 = sc[g + 8];
+    s[0] *= k0;
+    s[1] *= k0;
+    s[2] *= k1;
+    s[3] *= k1;
+  }
+  if (g >= valid) s[0] = s[1] = -INFINITY;
+  if (g + 8 >= valid) s[2] = s[3] = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float mx = fmaxf(s[r], s[2 + r]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mn = fmaxf(m[r], mx);
+    const float alpha = exp2f(m[r] - mn);
+    s[r] = exp2f(s[r] - mn);
+    s[2 + r] = exp2f(s[2 + r] - mn);
+    float sum = s[r] + s[2 + r];
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+    l[r] = l[r] * alpha + sum * kPScale;
+    m[r] = mn;
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) {
+      o[dt][r] *= alpha;
+      o[dt][2 + r] *= alpha;
+    }
+  }
+  const float v0 = g < valid ? sc[16 + g] * kPScale : 0.f, v1 = g + 8 < valid ? sc[24 + g] * kPScale : 0.f;
+  s[0] *= v0;
+  s[1] *= v0;
+  s[2] *= v1;
+  s[3] *= v1;
+  const uint32_t lo = pack_f16x2(s[0], s[1]), hi = pack_f16x2(s[2], s[3]);
+  const int src = 8 * t + (g >> 1);
+  const uint32_t x = __shfl_sync(0xffffffffu, lo, src), y = __shfl_sync(0xffffffffu, lo, src + 4);
+  const uint32_t z = __shfl_sync(0xffffffffu, hi, src), w = __shfl_sync(0xffffffffu, hi, src + 4);
+  const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
+  const uint32_t b0 = __byte_perm(x, y, sel), b1 = __byte_perm(z, w, sel);
+  const int row = (lane & 7) + ((lane >> 3) & 1) * 8, half = lane >> 4;
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    uint32_t r0, r1, r2, r3;
+    ldsm_x4_t(vt + k8_off<D>(row, 32 * j + 16 * half), r0, r1, r2, r3);
+    uint32_t a[4];
+    i8pairs_to_f16(r0, a[0], a[1]);
+    i8pairs_to_f16(r1, a[2], a[3]);
+    mma_f16(o[2 * j], a, b0, b1);
+    i8pairs_to_f16(r2, a[0], a[1]);
+    i8pairs_to_f16(r3, a[2], a[3]);
+    mma_f16(o[2 * j + 1], a, b0, b1);
+  }
+}
+
 template <int D>
 __device__ __forceinline__ void attend_tile_t(const uint32_t (&qb)[D / 16][2], uint32_t ks, uint32_t vs, int valid,
                                               float (&o)[D / 16][4], float (&m)[2], float (&l)[2], int lane,
@@ -519,18 +599,14 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
       if (!mbar_wait(&full[s], (i / kStages) & 1, 410)) break;
       const int valid = min(16, ctx - (b0 + i) * 16);
       if constexpr (Q8 && T) {
-        // V codes become this warp's bf16 tile and the scales are copied beside it; K is read from the stage
-        // itself, which is released once the score MMAs have consumed it
-        uint8_t* wb = smem + C::kBufOffset + warp * C::kBufBytes;
-        convert_stage<D>(smem, s, wb, valid, lane, 32, false);
-        __syncwarp();
+        // K and V codes go from the stage straight into f16 MMA fragments; the stage is released once the
+        // PV MMAs have consumed them
         float sct[4];
         scores_t8<D>(qa, smem_u32(smem + s * C::kTileBytes), sct, lane);
+        softmax_pv_t8<D>(sct, smem_u32(smem + C::kVRing + s * C::kTileBytes),
+                         reinterpret_cast<const float*>(smem + C::kSRing + s * 128), valid, o, m, l, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        softmax_pv_t<D>(sct, smem_u32(wb) + C::kBf16Tile, valid, o, m, l, lane,
-                        reinterpret_cast<const float*>(wb + 2 * C::kBf16Tile));
-        __syncwarp();  // every lane is done with the buffer before the next conversion
       } else if constexpr (Q8) {
         // the stage's codes become this warp's bf16 tiles; the stage is released once they are stored
         uint8_t* wb = smem + C::kBufOffset + warp * C::kBufBytes;
@@ -560,18 +636,24 @@ __device__ void private_cta(const AttnParams& p, const CUtensorMap* tk, const CU
   float* mg = reinterpret_cast<float*>(smem);
   const int c = (lane & 3) * 2;
   if (T && warp < kCons) {
-    // Oᵀ fragment (dims dt*16 + g0 (+8), heads c, c+1) -> rows = heads
+    // Oᵀ fragment (dims dt*16 + g0 (+8); Q8: dt*16 + 2g0 (+1)), heads c, c+1) -> rows = heads
+    constexpr float kUnscale = Q8 ? 1.f / kPScale : 1.f;  // exact: a power of two
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       float* dst = mg + (warp * 16 + c + r) * (D + 2);
 #pragma unroll
       for (int dt = 0; dt < kO; ++dt) {
-        dst[dt * 16 + g0] = o[dt][r];
-        dst[dt * 16 + g0 + 8] = o[dt][2 + r];
+        if constexpr (Q8) {
+          dst[dt * 16 + 2 * g0] = o[dt][r] * kUnscale;
+          dst[dt * 16 + 2 * g0 + 1] = o[dt][2 + r] * kUnscale;
+        } else {
+          dst[dt * 16 + g0] = o[dt][r];
+          dst[dt * 16 + g0 + 8] = o[dt][2 + r];
+        }
       }
       if (g0 == 0) {
         dst[D] = m[r];
-        dst[D + 1] = l[r];
+        dst[D + 1] = l[r] * kUnscale;
       }
     }
   } else if (warp < kCons) {
@@ -837,12 +919,12 @@ int launch_attn(AttnParams& p, const Plan& pl, const void* k_pool, const void* v
   if (rows > 0x7fffffffull) return MG_ERR_UNSUPPORTED;
   CUtensorMap tk, tv;
   int rc;
-  if constexpr (Q8) {  // int8 rows of d bytes, one box per tile; K swizzled for the consumers' ldmatrix reads
+  if constexpr (Q8) {  // int8 rows of d bytes, one box per tile, swizzled for the consumers' ldmatrix reads
     const CUtensorMapSwizzle ksw = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                             : (D == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
     rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_pool, D, rows, D, D, 16, ksw);
     if (rc) return rc;
-    rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_pool, D, rows, D, D, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = mg_make_map_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_pool, D, rows, D, D, 16, ksw);
   } else {
     const CUtensorMapSwizzle sw = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
     rc = mg_make_map_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k_pool, D, rows, D * 2, C::kBoxCols, 16, sw);

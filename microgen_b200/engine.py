@@ -543,10 +543,14 @@ class DecodeEngine:
         if not self.vocab_parallel:
             return self.logits[:b].clone()
         import torch.distributed as dist
-        mine = self.logits[:b].contiguous()
-        parts = [torch.empty_like(mine) for _ in range(self.world)]
-        dist.all_gather(parts, mine, group=self.group)
-        return torch.cat([p[:, :e - s_] for p, (s_, e) in zip(parts, vocab_bounds(self.spec.vocab, self.world))], 1)
+        mine = self.logits[:b]
+        width = mine.shape[1]
+        allv = torch.empty((self.world, b, width), dtype=mine.dtype, device=mine.device)
+        dist.all_gather_into_tensor(allv, mine, group=self.group)
+        bounds = vocab_bounds(self.spec.vocab, self.world)
+        if all(e - s_ == width for s_, e in bounds):  # equal shards: one transposing copy
+            return allv.transpose(0, 1).reshape(b, self.spec.vocab)
+        return torch.cat([allv[r, :, :e - s_] for r, (s_, e) in enumerate(bounds)], 1)
 
     # ---- prefill: many positions per launch ------------------------------------------------------
     PREFILL_CHUNK = 64

@@ -118,6 +118,39 @@ def test_tp2_matches_tp1(graph, fused, shape, block):
         assert clear.mean() > 0.3  # enough clear-margin steps for the argmax check to mean something
 
 
+# 16 query / 8 KV heads of 32: whole heads and 64-row gate/up groups on every rank up to TP=8
+SHAPE_W = dict(family="llama", hidden=512, layers=2, heads=16, kv_heads=8, head_dim=32, inter=2048, vocab=1024,
+               eps=1e-5, rope_theta=500000.0)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp_world_matches_tp1(world):
+    """TP=4 and TP=8 (fused push: every rank's bf16 partial summed in rank order, so 4 or 8 roundings per
+    element; vocab-parallel head) against TP=1, teacher-forced, as test_tp2_matches_tp1. Skipped without
+    that many GPUs."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    from microgen_b200.backends import B200QuantizedBackend
+    from tests._hf_models import make_hf_model
+    model, _ = make_hf_model(SHAPE_W, seed=0)
+    be = B200QuantizedBackend(max_batch=4, max_seq_len=128, free_list_seed=1)
+    be.load_model("tiny", model_instance=model)
+    ref_toks, ref_lg, _ = _decode(be, _prompts(SHAPE_W))
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_worker, args=(world, _port(), d, True, ref_toks, True, SHAPE_W, False), nprocs=world, join=True)
+        outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
+    tol = 1e-2 + 2e-2 * np.abs(ref_lg)
+    top2 = np.sort(ref_lg, axis=-1)[..., -2:]
+    clear = (top2[..., 1] - top2[..., 0]) > 2 * tol.max(axis=-1)
+    for toks, lg, _ in outs:
+        assert np.array_equal(lg, outs[0][1])
+        err = np.abs(lg - ref_lg)
+        assert not (err > tol).any(), f"max err {err.max():.3e}"
+        assert (np.argmax(lg, axis=-1) == np.argmax(ref_lg, axis=-1))[clear].all()
+    assert clear.mean() > 0.3
+
+
 def _ref_worker(rank, world, port, outdir, family):
     """TP=world over the reference's fixture model: greedy stream teacher-forced with the reference's tokens."""
     import json
@@ -167,5 +200,5 @@ def test_tp2_stream_matches_reference_fixture(family):
         top2 = np.sort(lg, axis=-1)[:, -2:]
         clear = (top2[:, 1] - top2[:, 0]) > 2 * (1e-2 + 2e-2 * np.abs(lg).max(axis=-1))
         assert (np.array(got) == ref_tok)[clear].all()
-        assert clear.mean() > 0.5
+        assert clear.mean() > 0.3  # enough clear-margin steps for the token check to mean something
     assert outs[0][0] == outs[1][0]  # every rank samples the same tokens
