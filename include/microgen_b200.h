@@ -125,7 +125,8 @@ int mg_rowpar_reduce_norm(void* comm, float* h, const float* bias, int m, int n,
  * [m, n_local] shard (row stride ld). Finds each row's first maximal local column, exchanges {value,
  * global index} with every rank through the communicator's receive areas (two epoch-tagged words per row,
  * the same epoch sequence as the row-parallel pushes, so every rank must make this call at the same point
- * of that sequence), and writes idx[i] = the global first maximal index of row i, identical on every rank.
+ * of that sequence), and writes idx[i] = the global first maximal index of row i, identical on every rank
+ * (NaN counts as larger than every number, as in torch.argmax: a row with a NaN gives its first NaN).
  * m <= 1024 and 2 * m <= slot words. A peer that never publishes makes the wait give up after the
  * communicator's limit (MG_ERR_TIMEOUT in the device error word). */
 int mg_vocab_argmax(void* comm, const float* logits, int m, int64_t n_local, int64_t ld, int64_t offset,
@@ -277,7 +278,8 @@ int mg_rmsnorm(const float* h, const float* w, int m, int n, float eps, void* x,
 /* x bf16 [m, n] = (h - mean) * rsqrt(var + eps) * w + bias  (GPT-2 LayerNorm) */
 int mg_layernorm(const float* h, const float* w, const float* bias, int m, int n, float eps, void* x,
                  void* stream);
-/* out[i] = first index of the maximum of logits fp32 row i (row stride ld) — torch.argmax. */
+/* out[i] = first index of the maximum of logits fp32 row i (row stride ld) — torch.argmax, NaN counting as
+ * larger than every number (a row with a NaN gives its first NaN; a row of -inf gives 0). */
 int mg_argmax_rows(const float* logits, int m, int64_t n, int64_t ld, int32_t* out, void* stream);
 /* One greedy step forward for a graph-replayed decode loop: tokens = next; positions += 1;
  * ctx_lens += 1; slots = table[pos/16]*16 + pos%16 for the new position. */

@@ -169,9 +169,9 @@ __global__ void __launch_bounds__(kThreads) rowpar_reduce_norm_kernel(PeerOut po
 // every row, in rank order. idx[i] enters as this rank's first maximal column of row i (mg_argmax_rows over
 // the shard). Each row's {value, global index} goes to slot [e%2][my rank] of every rank's receive area as two
 // words tagged with epoch e (e = this rank's count + 1, the same sequence the row-parallel pushes use); then
-// each row waits for the world's records (bounded by time), keeps the largest value, the smallest global
-// index on ties (torch.argmax's first maximal index over the whole row, pytorch.py:153-155), and the count
-// advances to e. One CTA, one thread per row.
+// each row waits for the world's records (bounded by time), keeps the largest value (NaN above every
+// number), the smallest global index on ties (torch.argmax's first maximal index over the whole row,
+// pytorch.py:153-155), and the count advances to e. One CTA, one thread per row.
 __global__ void __launch_bounds__(1024) vocab_argmax_merge_kernel(PeerOut po, const float* __restrict__ logits,
                                                                    int64_t ld, int64_t n_local, int64_t offset,
                                                                    int32_t* __restrict__ idx, int m) {
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(1024) vocab_argmax_merge_kernel(PeerOut po, co
       if (dead) break;
       const float rv = __uint_as_float((uint32_t)wd[r][0]);
       const int32_t ri = (int32_t)(uint32_t)wd[r][1];
-      if (rv > best || (rv == best && ri < bi)) {
+      if (mg_argmax_better(rv, ri, best, bi)) {
         best = rv;
         bi = ri;
       }

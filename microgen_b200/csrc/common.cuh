@@ -149,6 +149,13 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+// torch.argmax's order of (value, index) candidates: NaN above every number, equal values (or two
+// NaNs) by the smaller index. True when (v, i) comes before (best, bi).
+__device__ __forceinline__ bool mg_argmax_better(float v, int32_t i, float best, int32_t bi) {
+  const bool vn = v != v, bn = best != best;
+  if (vn != bn) return vn;
+  return (!vn && v > best) || ((vn || v == best) && i < bi);
+}
 
 // bf16x2 word -> two floats (exact: bf16 is the upper half of an fp32)
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }

@@ -279,14 +279,15 @@ __global__ void rope_kv_append_kv8_kernel(const float* __restrict__ qkv, int64_t
   if (j == 0) (is_k ? k_scales : v_scales)[row] = sc;
 }
 
-// torch.argmax semantics: the first index holding the maximum. A row is split over a cluster of
-// kArgSplit CTAs (contiguous chunks, float4 loads where the row is 16-byte aligned); CTA 0 of the
-// cluster merges the chunk results through distributed shared memory, smaller index on ties.
+// torch.argmax semantics: the first index holding the maximum, NaN counting as larger than every
+// number (a row with a NaN gives its first NaN). A row is split over a cluster of kArgSplit CTAs
+// (contiguous chunks, float4 loads where the row is 16-byte aligned); CTA 0 of the cluster merges the
+// chunk results through distributed shared memory, smaller index on ties.
 constexpr int kArgSplit = 8;
 constexpr int kArgThreads = 512;
 
 __device__ __forceinline__ void argmax_take(float v, int32_t i, float& best, int32_t& bi) {
-  if (v > best || (v == best && i < bi)) {
+  if (mg_argmax_better(v, i, best, bi)) {
     best = v;
     bi = i;
   }
@@ -322,10 +323,10 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* __rest
     for (int64_t j = threadIdx.x; j < nv; j += kArgThreads) {
       const float4 v = r4[j];
       const int32_t k = (int32_t)(lo + 4 * j);
-      if (v.x > best) { best = v.x; bi = k; }
-      if (v.y > best) { best = v.y; bi = k + 1; }
-      if (v.z > best) { best = v.z; bi = k + 2; }
-      if (v.w > best) { best = v.w; bi = k + 3; }
+      argmax_take(v.x, k, best, bi);
+      argmax_take(v.y, k + 1, best, bi);
+      argmax_take(v.z, k + 2, best, bi);
+      argmax_take(v.w, k + 3, best, bi);
     }
     i0 = lo + 4 * nv;
   }

@@ -124,17 +124,16 @@ def vocab_bounds(vocab: int, world: int) -> list[tuple[int, int]]:
 def merge_vocab_argmax(val: torch.Tensor, gidx: torch.Tensor, world: int, group=None) -> torch.Tensor:
     """Global greedy token of a vocab-parallel lm_head over a process group (the NCCL form of
     ``mg_vocab_argmax``): ``val`` fp32 [b] and ``gidx`` int32 [b] are this rank's maximal logit and its global
-    column. All ranks' pairs are gathered; each row takes the largest value and, on ties, the lowest rank,
-    whose columns come first — torch.argmax's first maximal index over the whole row (``pytorch.py:153-155``).
-    NaN never wins, as in the local argmax kernel."""
+    column. All ranks' pairs are gathered; each row takes the largest value (NaN above every number) and, on
+    ties, the lowest rank, whose columns come first — torch.argmax's first maximal index over the whole row
+    (``pytorch.py:153-155``), as the local argmax kernel keeps it within a shard."""
     import torch.distributed as dist
     rec = torch.stack([val.contiguous().view(torch.int32), gidx.to(torch.int32)], 1)
     parts = [torch.empty_like(rec) for _ in range(world)]
     dist.all_gather(parts, rec, group=group)
     allr = torch.stack(parts)                                   # [world, b, 2]
     vals = allr[..., 0].contiguous().view(torch.float32)
-    vals = torch.where(torch.isnan(vals), torch.full_like(vals, float("-inf")), vals)
-    r = vals.argmax(0)                                          # first maximal rank
+    r = vals.argmax(0)                                          # first maximal rank (NaN first, as torch)
     return allr[r, torch.arange(allr.shape[1], device=allr.device), 1]
 
 

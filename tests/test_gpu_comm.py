@@ -135,6 +135,7 @@ def test_world1_vocab_argmax_matches_local_argmax():
             K.rowpar_reduce_norm(comm, h, d(bias), 0)
             lg = _vocab_logits(m, 1000 + rep, seed=rep)
             want = K.argmax_rows(lg).cpu()
+            assert torch.equal(want, lg.cpu().argmax(1).to(want.dtype))  # torch.argmax, NaN rows included
             got = K.vocab_argmax(comm, lg, 0).cpu()
             assert torch.equal(got, want), (got, want)
             # a column slice with a row stride > its width, as the engine's shard buffer is

@@ -206,15 +206,24 @@ def test_rope_kv_append(hq, hkv, d):
 
 
 def test_argmax_first_max_index():
+    """torch.argmax's answer (numpy's argmax agrees): the first maximal index; NaN counts as larger than
+    every number, so a row with NaNs gives its first NaN; a row of -inf gives 0."""
     rng = np.random.default_rng(5)
-    lg = rng.standard_normal((6, 128256)).astype(np.float32)
+    lg = rng.standard_normal((11, 128256)).astype(np.float32)
     lg[1, 77] = lg[1, 1000] = 50.0     # tie -> first index
     lg[2, :] = 0.0
     lg[3, -1] = 99.0
     lg[4, 5] = lg[4, 100000] = 60.0    # tie across the row's chunks
     lg[5, 128255] = 70.0               # last element
+    lg[6, 90000] = np.nan              # a NaN after the row's maximum
+    lg[6, 10] = 80.0
+    lg[7, 70001] = lg[7, 3] = np.nan   # NaNs in two chunks: the first one
+    lg[8, :] = np.nan
+    lg[9, :] = -np.inf
+    lg[10, 128255] = np.nan            # the last element, float4 path
     out = K().argmax_rows(dev(lg)).cpu().numpy()
     assert out.tolist() == np.argmax(lg, axis=1).tolist()
+    assert out.tolist() == torch.from_numpy(lg).argmax(1).tolist()
 
 
 @pytest.mark.parametrize("n,ld", [(5, 5), (31, 33), (1000, 1003), (50257, 50257), (50257, 50260)])
@@ -225,6 +234,9 @@ def test_argmax_short_and_unaligned_rows(n, ld):
     full[0, n - 1] = 40.0
     full[1, 0] = 40.0
     full[2, :n] = 1.0
+    full[3, n // 2] = np.nan
+    full[3, n - 1] = np.nan
+    full[4, :n] = -np.inf
     lgd = dev(full)[:, :n]
     out = K().argmax_rows(lgd).cpu().numpy()
     assert out.tolist() == np.argmax(full[:, :n], axis=1).tolist()

@@ -179,13 +179,14 @@ def _merge_worker(rank, world, port, outdir, vocab, seed):
     full[1] = float("-inf")                        # no finite value: torch.argmax gives 0
     full[2, :] = 0.0
     full[2, vocab - 1] = 5.0                       # the maximum in the last rank's shard
-    full[3, :] = float("nan")                      # NaN never wins; all NaN gives 0
+    full[3, :] = float("nan")                      # NaN is larger than every number: the first NaN
     full[4, ::3] = float("nan")
+    full[5, :] = 1.0
+    full[5, vocab - 2] = float("nan")              # the only NaN, in the last rank's shard
     a, e = vocab_bounds(vocab, world)[rank]
     shard = full[:, a:e]
-    clean = torch.where(torch.isnan(shard), torch.full_like(shard, float("-inf")), shard)
-    li = clean.argmax(1)                           # local first maximal column (NaN skipped)
-    val = clean.gather(1, li[:, None])[:, 0]
+    li = shard.argmax(1)                           # local first maximal column, as the argmax kernel
+    val = shard.gather(1, li[:, None])[:, 0]
     got = merge_vocab_argmax(val, (li + a).to(torch.int32), world, dist.group.WORLD)
     torch.save({"got": got, "full": full}, os.path.join(outdir, f"r{rank}.pt"))
     dist.destroy_process_group()
@@ -194,11 +195,10 @@ def _merge_worker(rank, world, port, outdir, vocab, seed):
 @pytest.mark.parametrize("world,vocab", [(2, 37), (3, 50), (4, 64)])
 def test_merge_vocab_argmax_matches_full_argmax(world, vocab):
     """The NCCL-path merge of per-rank (max, global index) pairs equals torch.argmax over the whole row:
-    ties across shards go to the first index, -inf rows to 0, NaN ignored (all-NaN rows give 0)."""
+    ties across shards go to the first index, -inf rows to 0, a row with NaNs to its first NaN."""
     outs = _run(_merge_worker, world, vocab, 5)
     full = outs[0]["full"]
-    clean = torch.where(torch.isnan(full), torch.full_like(full, float("-inf")), full)
-    want = clean.argmax(1).to(torch.int32)
-    want[3] = 0
+    want = full.argmax(1).to(torch.int32)
+    assert want[5] == vocab - 2 and want[3] == 0
     for o in outs:
         assert torch.equal(o["got"], want), (o["got"], want)
