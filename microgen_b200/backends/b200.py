@@ -28,6 +28,7 @@ from __future__ import annotations
 
 from typing import Any, Dict, List, Optional, Tuple
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -193,16 +194,19 @@ class B200QuantizedBackend:
              logits: bool, cache_mirror: Optional[TableMirror] = None) -> None:
         eng = self.engine
         b = len(tables)
-        slots = [t.slot(p) for t, p in zip(tables, positions)]
-        ctx = [p + 1 for p in positions]
-        width = max(t.num_blocks() for t in tables)
-        if width > eng.max_blocks:
+        if max(t.num_blocks() for t in tables) > eng.max_blocks:
+            width = max(t.num_blocks() for t in tables)
             raise ValueError(f"context of {width * BLOCK} tokens exceeds max_seq_len {self.max_seq_len}")
         if cache_mirror is None:
             cache_mirror = TableMirror(b, eng.max_blocks)
         tab = cache_mirror.update(tables)
-        check_shared_prefix(tab, n_shared)
-        eng.set_inputs(tokens, positions, slots, ctx, tab)
+        key = (cache_mirror.rebuilds, b, n_shared)
+        if cache_mirror.prefix_checked != key:  # rows only grew since the last check: leading entries kept
+            check_shared_prefix(tab, n_shared)
+            cache_mirror.prefix_checked = key
+        pos = np.asarray(positions, dtype=np.int64)
+        slots = tab[np.arange(b), pos // BLOCK].astype(np.int64) * BLOCK + pos % BLOCK
+        eng.set_inputs(tokens, pos, slots, pos + 1, tab)
         if self.use_cuda_graph:
             eng.capture(b, n_shared, compute_logits=logits).replay()
         else:
@@ -279,10 +283,11 @@ class B200QuantizedBackend:
 
     def _logits_out(self, b: int) -> torch.Tensor:
         """The step's full logits for the caller, remembering the greedy tokens the step already computed
-        on the device so that ``sample`` of these unmodified logits needs no second argmax."""
+        on the device (as int64 [b, 1], sample's return type) so that the first ``sample`` of these
+        unmodified logits needs no second argmax."""
         eng = self.engine
         out = eng.full_logits(b)
-        self._greedy = (out, out._version, eng.next_tokens[:b].clone())
+        self._greedy = (out, out._version, eng.next_tokens[:b, None].to(torch.int64))
         return out
 
     def decode(self, token_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
@@ -302,10 +307,11 @@ class B200QuantizedBackend:
             if cache.mirror is None or cache.mirror.arr.shape[0] < b:
                 cache.mirror = TableMirror(b, eng.max_blocks)
             self._run(cache.tables, toks, positions, cache.n_shared_blocks, logits=True, cache_mirror=cache.mirror)
+            out = self._logits_out(b)  # the copies queue behind the step, ahead of the check's synchronisation
             self._decodes += 1
             if self.device_check_every and self._decodes % self.device_check_every == 0:
                 K.check_device()
-            return self._logits_out(b), cache
+            return out, cache
 
     def sample(self, logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0,
                top_p: float = 0.0) -> torch.Tensor:
@@ -313,7 +319,8 @@ class B200QuantizedBackend:
         if temperature <= 0.0 or (top_k == 0 and top_p == 0.0 and temperature == 1.0):
             g = self._greedy
             if g is not None and logits is g[0] and logits._version == g[1]:
-                return g[2].to(torch.int64)[:, None]  # the device argmax of exactly these logits
+                self._greedy = None  # handed out once: a later call returns a new tensor, as torch.argmax does
+                return g[2]  # the device argmax of exactly these logits
             lg = logits.to(torch.float32).contiguous()
             return K.argmax_rows(lg).to(torch.int64)[:, None]
         logits = logits / max(temperature, 1e-5)

@@ -162,13 +162,16 @@ class TableMirror:
     A decode step appends at most one block per sequence, so rebuilding the whole table in Python
     every step (hundreds of microseconds for a batch of 32) is replaced by writing the new entries.
     A row is rebuilt when its table object changes, its ``version`` changes (blocks removed), or its
-    last mirrored entry no longer matches. Entries past a row's block count are zero."""
+    last mirrored entry no longer matches. Entries past a row's block count are zero. ``rebuilds`` counts
+    row rebuilds: while it is unchanged, every row's existing entries are unchanged (rows only grew)."""
 
     def __init__(self, rows: int, max_blocks: int) -> None:
         self.arr = np.zeros((rows, max_blocks), np.int32)
         self._tabs: List[Optional[BlockTable]] = [None] * rows
         self._ver = [0] * rows
         self._n = [0] * rows
+        self.rebuilds = 0
+        self.prefix_checked = None  # (rebuilds, rows, shared blocks) of the last shared-prefix check passed
 
     def update(self, tables: Sequence[BlockTable]) -> np.ndarray:
         """The mirror's rows for ``tables`` (a view, [len(tables), widest table])."""
@@ -186,6 +189,7 @@ class TableMirror:
                 self.arr[i, :n] = 0
                 self._tabs[i], self._ver[i], n = t, t.version, 0
                 self._n[i] = 0
+                self.rebuilds += 1
             if nb > n:
                 self.arr[i, n:nb] = [b.block_id for b in blocks[n:nb]]
             self._n[i] = nb

@@ -133,3 +133,29 @@ def test_check_shared_prefix():
     t[2, 1] = 9
     with pytest.raises(ValueError, match="sequence 2"):
         check_shared_prefix(t, 2)
+
+
+def test_mirror_rebuild_count_tracks_changed_rows():
+    """Rows that only grow keep ``rebuilds``; a rollback that frees blocks or a replaced table raises it.
+    The decode step re-checks the shared-prefix contract only when ``rebuilds`` moved."""
+    a = PagedKVCacheAllocator(num_blocks=64)
+    s0, s1 = a.allocate_sequence("s0", 40), a.allocate_sequence("s1", 20)
+    m = TableMirror(2, 16)
+    m.update([s0, s1])
+    r0 = m.rebuilds
+    for _ in range(40):
+        a.append_token(s0)
+        a.append_token(s1)
+        tab = m.update([s0, s1])
+    assert m.rebuilds == r0
+    assert tab[0, :s0.num_blocks()].tolist() == s0.block_ids()
+    assert tab[1, :s1.num_blocks()].tolist() == s1.block_ids()
+    a.rollback(s0, 3)                      # frees no block: entries unchanged, no rebuild
+    m.update([s0, s1])
+    assert m.rebuilds == r0
+    a.rollback(s0, 30)                     # frees blocks
+    assert m.update([s0, s1])[0, :s0.num_blocks()].tolist() == s0.block_ids()
+    assert m.rebuilds == r0 + 1
+    s2 = a.allocate_sequence("s2", 5)
+    assert m.update([s2, s1])[0].tolist()[:2] == s2.block_ids() + [0]
+    assert m.rebuilds == r0 + 2
