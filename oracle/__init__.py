@@ -17,6 +17,9 @@ the path the CUDA library accelerates:
                   (Llama / Qwen2 / GPT-2 shapes), restating the forward of
                   transformers 5.5.0 (``modeling_llama.py``, ``modeling_qwen2.py``,
                   ``modeling_gpt2.py``) with the quantized linears swapped in.
+* ``cpu_baseline`` — not a checker: the reference's CPU decode step restated with
+                  the same torch CPU operations it runs, for timing only
+                  (``port_vs_reference_timing.py`` compares it with the reference).
 
 Pinning: ``tests/test_oracle_golden.py`` checks every function here against
 fixtures under ``tests/golden/`` that ``tests/golden/make_golden.py`` produced by

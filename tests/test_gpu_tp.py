@@ -202,3 +202,69 @@ def test_tp2_stream_matches_reference_fixture(family):
         assert (np.array(got) == ref_tok)[clear].all()
         assert clear.mean() > 0.3  # enough clear-margin steps for the token check to mean something
     assert outs[0][0] == outs[1][0]  # every rank samples the same tokens
+
+
+def _argmax_rows_world(vocab):
+    """fp32 rows whose first maximal index needs both shards of a 2-way vocab split (columns [0, vocab//2)
+    and [vocab//2, vocab)): ties within and across shards, -inf rows, and NaN (larger than every number
+    for torch.argmax) in one shard, both, or everywhere."""
+    g = torch.Generator().manual_seed(4)
+    full = torch.randint(-3, 4, (8, vocab), generator=g).float()
+    h = vocab // 2
+    full[1] = float("-inf")
+    full[2, :] = 0.0
+    full[2, vocab - 1] = 3.0                  # the maximum is the last rank's last column
+    full[3, 5] = 100.0
+    full[3, h + 200] = float("nan")            # NaN only in the second shard beats a larger number
+    full[4, h + 1] = float("nan")
+    full[4, 17] = float("nan")                 # NaN in both shards: the first one
+    full[5, :] = 1.0
+    full[5, 10] = full[5, h + 100] = 9.0       # a tie across shards: the first index
+    full[6] = float("nan")
+    full[7, :] = 0.0
+    full[7, h - 1] = full[7, h] = 2.0          # a tie on both sides of the shard boundary
+    return full
+
+
+def _vocab_argmax_worker(rank, world, port, outdir):
+    import torch.distributed as dist
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from microgen_b200 import kernels as K
+    from microgen_b200.engine import vocab_bounds
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    vocab = 1001
+    full = _argmax_rows_world(vocab)
+    a, e = vocab_bounds(vocab, world)[rank]
+    comm = K.Comm(rank, world, 8 * 256, group=dist.group.WORLD)
+    got = []
+    try:
+        wide = torch.zeros((8, e - a + 5), device="cuda")
+        wide[:, :e - a] = full[:, a:e].cuda()
+        for _ in range(3):  # consecutive exchanges alternate the receive sets
+            got.append(K.vocab_argmax(comm, full[:, a:e].cuda(), a).cpu())
+            got.append(K.vocab_argmax(comm, wide[:, :e - a], a).cpu())  # a row stride wider than the shard
+        K.check_device()
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        comm.close()
+    torch.save(got, os.path.join(outdir, f"r{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_vocab_argmax_world2_matches_torch_argmax():
+    """``mg_vocab_argmax`` across two GPUs equals torch.argmax over the whole row on every rank: ties across
+    shards go to the first index, -inf rows to 0, NaN counts as larger than every number."""
+    import torch.multiprocessing as mp
+    want = _argmax_rows_world(1001).argmax(1).to(torch.int32)
+    assert want.tolist()[1:] == [0, 1000, 700, 17, 10, 0, 499]
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_vocab_argmax_worker, args=(2, _port(), d), nprocs=2, join=True)
+        outs = [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(2)]
+    for got in outs:
+        for g in got:
+            assert torch.equal(g.to(torch.int32), want), (g, want)
