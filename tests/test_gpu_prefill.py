@@ -97,3 +97,40 @@ def test_chunked_prefill_single_prompt_and_greedy_token():
     lg1, _ = new.prefill(torch.tensor(prompt))
     _close(lg1.cpu().numpy(), lg0.cpu().numpy(), "prompt logits")
     assert new.sample(lg1).item() == int(np.argmax(lg1.cpu().numpy()[0]))
+
+
+@pytest.mark.parametrize("chunk", [0, 64])
+def test_prefix_cache_reuses_blocks_across_prefills(chunk):
+    """``prefix_cache_capacity``: a prefill caches its prompt's whole leading blocks; a later prefill whose
+    prompt starts with them shares those blocks (no recompute) and gives the logits and decode steps of a
+    backend without the cache. The first request's cache is freed before the later prefills and other
+    blocks are allocated in between, so the shared blocks survive only through the prefix cache's own
+    references."""
+    shape = TINY["llama"]
+    model, _ = make_hf_model(shape, seed=4)
+    V = shape["vocab"]
+    from microgen_b200.backends import B200QuantizedBackend
+    be = B200QuantizedBackend(max_batch=4, max_seq_len=160, free_list_seed=5, prefill_chunk=chunk,
+                              prefix_cache_capacity=8)
+    be.load_model("tiny", model_instance=model)
+    ref = _backend(model, chunk)
+    s = prompt_ids(V, 48, seed=11)                          # three whole blocks
+    _, c1 = be.prefill(torch.tensor([s + prompt_ids(V, 5, seed=12)]))
+    cached = c1.tables[0].block_ids()[:3]
+    c1.free()
+    _, other = be.prefill(torch.tensor([prompt_ids(V, 70, seed=13)] * 2))  # takes the freed private blocks
+    for prompts in ([s + prompt_ids(V, 20, seed=14)], [s + prompt_ids(V, 12, seed=15), s + prompt_ids(V, 12, seed=16)]):
+        lg1, c2 = be.prefill(torch.tensor(prompts))
+        lg0, c0 = ref.prefill(torch.tensor(prompts))
+        assert c2.reused_prefix_tokens == 48
+        assert all(t.block_ids()[:3] == cached for t in c2.tables)
+        _close(lg1.cpu().numpy(), lg0.cpu().numpy(), "prompt logits")
+        tok = ref.sample(lg0)
+        for step in range(4):
+            lg0, c0 = ref.decode(tok, cache=c0)
+            lg1, c2 = be.decode(tok, cache=c2)
+            _close(lg1.cpu().numpy(), lg0.cpu().numpy(), f"decode step {step}")
+            tok = ref.sample(lg0)
+        c0.free()
+        c2.free()
+    other.free()
