@@ -508,8 +508,18 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def host_threads() -> int:
+    """Give torch's CPU ops every host CPU this process may run on (torchrun sets OMP_NUM_THREADS=1 in its
+    workers, which would time the CPU legs on one thread) and return that count."""
+    import torch
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return n
+
+
 def cpu_baseline(spec, wl, ctx, budget_s=20.0) -> dict:
     from oracle.cpu_baseline import measure
+    host_threads()
     r = measure(spec.hidden, spec.heads, spec.kv_heads, spec.head_dim, spec.inter, spec.vocab, spec.layers,
                 wl["batch"], ctx, budget_s=budget_s, eps=spec.eps, theta=spec.rope_theta)
     return {"value": round(r["tokens_per_s"], 4), "unit": "tokens/s", "cores": r["threads"], "kind": "port",
@@ -540,6 +550,7 @@ def run_reference(args) -> None:
         return
     from microgen_b200 import model_spec as MS
     from oracle.cpu_baseline import measure_steps
+    host_threads()
     wl = WORKLOADS[args.workload]
     spec = MS.ModelSpec(**getattr(MS, wl["shape"]))
     ctx = wl["prompt"] + wl["decode"] // 2
