@@ -5,6 +5,7 @@ TP=1 greedy stream: logits must agree within the bf16 tolerance at every step, a
 wherever TP=1's top-1/top-2 margin exceeds that tolerance (TP sums the row-parallel partials in another
 order, so only near-ties may flip). Skipped when fewer than two GPUs are visible."""
 
+import datetime
 import os
 import socket
 import tempfile
@@ -18,6 +19,7 @@ pytestmark = pytest.mark.gpu
 SHAPE = dict(family="llama", hidden=512, layers=2, heads=8, kv_heads=4, head_dim=64, inter=1024, vocab=1024,
              eps=1e-5, rope_theta=500000.0)
 N_NEW = 24
+PG_TIMEOUT = datetime.timedelta(seconds=120)  # ranks that wait on a dead peer end with an error
 
 
 def _port():
@@ -61,7 +63,7 @@ def _worker(rank, world, port, outdir, graph, forced, fused, shape=SHAPE, block=
     from tests._hf_models import make_hf_model
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank), timeout=PG_TIMEOUT)
     model, _ = make_hf_model(shape, seed=0)
     be = B200TensorParallelBackend(world_size=world, group=dist.group.WORLD, max_batch=4, max_seq_len=128,
                                    use_cuda_graph=graph, free_list_seed=1)
@@ -160,7 +162,7 @@ def _ref_worker(rank, world, port, outdir, family):
     from tests._hf_models import make_hf_model
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank), timeout=PG_TIMEOUT)
     d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", f"model_{family}.npz"))
     model, _ = make_hf_model(json.loads(str(d["shape"])), seed=0)
     be = B200TensorParallelBackend(world_size=world, group=dist.group.WORLD, max_batch=1, max_seq_len=128)
@@ -233,7 +235,7 @@ def _vocab_argmax_worker(rank, world, port, outdir):
     from microgen_b200.engine import vocab_bounds
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank), timeout=PG_TIMEOUT)
     vocab = 1001
     full = _argmax_rows_world(vocab)
     a, e = vocab_bounds(vocab, world)[rank]

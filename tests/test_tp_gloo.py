@@ -8,6 +8,7 @@
   codes exactly (codes from the oracle quantizer, as the device kernel produces them).
 """
 
+import datetime
 import os
 import socket
 import tempfile
@@ -33,7 +34,8 @@ def _run(fn, world, *args):
 
 
 def _init(rank, world, port):
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
 
 
 def _protocol_worker(rank, world, port, outdir):
